@@ -1,0 +1,6 @@
+"""Stage-level ops of the CAB prefill path (each backed by one C-ABI entry point)."""
+
+from .coarsening import coarsen_max_l2, coarsen_qk_max_l2, coarsen_qk_max_l2_pytorch  # noqa: F401
+from .frc_kernel import (compute_block_frc, generate_block_mask, keep_count,  # noqa: F401
+                         topk_blocks, visualize_frc_statistics)
+from .sparse_attention import block_sparse_attention  # noqa: F401

@@ -1,0 +1,718 @@
+// K4: block-sparse attention forward over the kept key blocks.
+//
+// Tensor-core path (bf16/f16, block_size 64, D in {64, 128}):
+//  * Work item = (b, query head h, pair p): the 128 query rows of query blocks 2p and
+//    2p+1, the M=128 shape of tcgen05.mma. The two rows' kept-block lists are merged by
+//    `pair_union_kernel` into one ascending list whose entries carry two flags (kept by
+//    block 2p / by block 2p+1); key blocks are consumed two at a time (a 128-key tile).
+//    A block kept by only one of the two query blocks is masked for the other 64 rows.
+//  * Warp 0 streams Q (once per item), K and V tiles with TMA (128-byte swizzle) into
+//    3/2-stage (D=128) or 4/4-stage (D=64) shared-memory rings. One thread of warp 1
+//    issues S = Q K^T (M=128, N=128, K=D) into one of two TMEM S buffers and, one tile
+//    behind, O += P V (M=128, N=D, K=128, V read MN-major straight from its natural
+//    [keys, D] layout) into a TMEM O accumulator, so S(t+1) overlaps the softmax of t.
+//  * Warps 2-5 own one query row per thread: tcgen05.ld of the S row, exact masking
+//    (flags, causal token mask, sequence end), online softmax in the exp2 domain with a
+//    lazy rescale of O (only when the running max grows by more than 2^8), P written as
+//    bf16/f16 into a 128-byte-swizzled shared tile, and the final O / l epilogue.
+//  * Items run (b, h, p)-major so the CTAs in flight share one head's K/V in L2.
+//
+// CUDA-core path: one CTA per query block, fp32 arithmetic, any dtype, block <= 128,
+// D <= 128.
+//
+// Semantics: softmax over the kept blocks' keys with -inf elsewhere, fully masked rows
+// -> 0 (manual sparse path of the reference: experiments/longbench_qa/methods.py:103-119
+// expands the block mask, :348-356 masks, softmaxes and applies nan_to_num).
+
+#include "cab_host.h"
+#include "cab_ptx.cuh"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cmath>
+
+namespace cab {
+namespace attn {
+
+constexpr uint32_t kIdxMask = 0x3FFFFFFFu;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// ------------------------------------------------------------------ pair union lists
+struct UnionParams {
+  const int32_t* kv_idx;
+  const int32_t* kv_num;
+  uint32_t* ulist;   // [items, stride]
+  int32_t* ntiles;   // [items]
+  int64_t items;     // B*Hq*P
+  int32_t M, P, kmax, stride, words;
+};
+
+__global__ void __launch_bounds__(128) pair_union_kernel(const UnionParams p) {
+  extern __shared__ uint32_t bm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint32_t* b0 = bm + static_cast<size_t>(warp) * 2 * p.words;
+  uint32_t* b1 = b0 + p.words;
+  for (int64_t item = static_cast<int64_t>(blockIdx.x) * 4 + warp; item < p.items;
+       item += static_cast<int64_t>(gridDim.x) * 4) {
+    const int64_t bh = item / p.P;
+    const int pr = static_cast<int>(item % p.P);
+    for (int w = lane; w < 2 * p.words; w += 32) b0[w] = 0u;
+    __syncwarp();
+    for (int half = 0; half < 2; ++half) {
+      const int i = 2 * pr + half;
+      if (i >= p.M) continue;
+      const int64_t row = bh * p.M + i;
+      const int n = min(max(p.kv_num[row], 0), p.kmax);
+      uint32_t* bits = half ? b1 : b0;
+      for (int x = lane; x < n; x += 32) {
+        const int j = p.kv_idx[row * p.kmax + x];
+        if (j >= 0 && j < p.M) atomicOr(&bits[j >> 5], 1u << (j & 31));
+      }
+    }
+    __syncwarp();
+    uint32_t* out = p.ulist + item * p.stride;
+    int total = 0;
+    for (int base = 0; base < p.words; base += 32) {
+      const int w = base + lane;
+      const uint32_t x0 = w < p.words ? b0[w] : 0u, x1 = w < p.words ? b1[w] : 0u;
+      uint32_t u = x0 | x1;
+      const int cnt = __popc(u);
+      int incl = cnt;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += o;
+      }
+      int pos = total + incl - cnt;
+      while (u) {
+        const int bit = __ffs(u) - 1;
+        u &= u - 1;
+        out[pos++] = static_cast<uint32_t>(32 * w + bit) | (((x0 >> bit) & 1u) << 30) |
+                     (((x1 >> bit) & 1u) << 31);
+      }
+      total += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      if (total & 1) out[total] = out[total - 1] & kIdxMask;  // padding block, masked for all rows
+      p.ntiles[item] = (total + 1) / 2;
+    }
+    __syncwarp();
+  }
+}
+
+// ------------------------------------------------------------------ tensor-core kernel
+template <int D>
+struct Cfg {
+  static constexpr int kAtoms = D / 64;
+  static constexpr int kQBytes = 128 * D * 2;
+  static constexpr int kKBytes = 128 * D * 2;
+  static constexpr int kVBytes = 128 * D * 2;
+  static constexpr int kPBytes = 128 * 128 * 2;
+  static constexpr int kKStages = D == 128 ? 3 : 4;
+  static constexpr int kVStages = D == 128 ? 2 : 4;
+  static constexpr int kTileBytes = kQBytes + kKStages * kKBytes + kVStages * kVBytes + kPBytes;
+  static constexpr int kSmem = kTileBytes + 1024 + 512;
+};
+
+struct Params {
+  int32_t B, Hq, Hkv, N, M, P;
+  int64_t items;
+  int64_t o_s0, o_s1, o_s2;
+  void* out;
+  float* lse;
+  const uint32_t* ulist;
+  const int32_t* ntiles;
+  int32_t stride;
+  float scale_log2;
+  int32_t causal;
+};
+
+template <int D, bool kBF16>
+__global__ void __launch_bounds__(192, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                   const __grid_constant__ CUtensorMap vmap, const Params p) {
+  using C = Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = base;
+  uint8_t* sK = sQ + C::kQBytes;
+  uint8_t* sV = sK + C::kKStages * C::kKBytes;
+  uint8_t* sP = sV + C::kVStages * C::kVBytes;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sP + C::kPBytes);
+  uint64_t* q_full = bar;
+  uint64_t* q_empty = bar + 1;
+  uint64_t* k_full = bar + 2;
+  uint64_t* k_empty = k_full + C::kKStages;
+  uint64_t* v_full = k_empty + C::kKStages;
+  uint64_t* v_empty = v_full + C::kVStages;
+  uint64_t* s_full = v_empty + C::kVStages;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_free + 2;
+  uint64_t* o_ready = p_full + 1;
+  uint64_t* o_free = o_ready + 1;
+  uint64_t* drain = o_free + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&qmap);
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int s = 0; s < C::kKStages; ++s) { mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1); }
+    for (int s = 0; s < C::kVStages; ++s) { mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1); }
+    for (int s = 0; s < 2; ++s) { mbar_init(&s_full[s], 1); mbar_init(&s_free[s], 4); }
+    mbar_init(p_full, 4);
+    mbar_init(o_ready, 1);
+    mbar_init(o_free, 4);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_o = tmem + 256;
+  const int G = p.Hq / p.Hkv;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t gi = 0, kt = 0, vt = 0;
+      bool ok = true;
+      for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
+        const int T = p.ntiles[item];
+        if (T == 0) continue;
+        const int bh = static_cast<int>(item / p.P), pr = static_cast<int>(item % p.P);
+        const int b = bh / p.Hq, h = bh % p.Hq, hk = h / G;
+        const uint32_t* ul = p.ulist + item * p.stride;
+        if (!mbar_wait(q_empty, (gi & 1) ^ 1, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(q_full, C::kQBytes);
+#pragma unroll
+        for (int a = 0; a < C::kAtoms; ++a) tma_load_4d(sQ + a * 16384, &qmap, q_full, 64 * a, 128 * pr, h, b);
+        for (int t = 0; t < T; ++t) {
+          const int j0 = static_cast<int>(ul[2 * t] & kIdxMask), j1 = static_cast<int>(ul[2 * t + 1] & kIdxMask);
+          const int ks = kt % C::kKStages;
+          if (!mbar_wait(&k_empty[ks], ((kt / C::kKStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&k_full[ks], C::kKBytes);
+          uint8_t* dk = sK + ks * C::kKBytes;
+#pragma unroll
+          for (int a = 0; a < C::kAtoms; ++a) {
+            tma_load_4d(dk + a * 16384, &kmap, &k_full[ks], 64 * a, 64 * j0, hk, b);
+            tma_load_4d(dk + a * 16384 + 8192, &kmap, &k_full[ks], 64 * a, 64 * j1, hk, b);
+          }
+          ++kt;
+          const int vs = vt % C::kVStages;
+          if (!mbar_wait(&v_empty[vs], ((vt / C::kVStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&v_full[vs], C::kVBytes);
+          uint8_t* dv = sV + vs * C::kVBytes;
+#pragma unroll
+          for (int a = 0; a < C::kAtoms; ++a) {
+            tma_load_4d(dv + a * 16384, &vmap, &v_full[vs], 64 * a, 64 * j0, hk, b);
+            tma_load_4d(dv + a * 16384 + 8192, &vmap, &v_full[vs], 64 * a, 64 * j1, hk, b);
+          }
+          ++vt;
+        }
+        ++gi;
+      }
+      if (!ok) {
+        // bounded drain of the loads this thread may still have in flight
+        (void)mbar_wait(q_full, (gi & 1), nullptr);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = make_idesc_f16(128, 128, kBF16 ? 1 : 0, 0, 0);
+      constexpr uint32_t idesc_o = make_idesc_f16(128, D, kBF16 ? 1 : 0, 0, 1);
+      const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
+      uint32_t gi = 0, kt = 0, vt = 0, gt = 0;
+      bool ok = true;
+      for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
+        const int T = p.ntiles[item];
+        if (T == 0) continue;
+        if (!mbar_wait(q_full, gi & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after_sync();
+        for (int t = 0; t <= T && ok; ++t) {
+          if (t < T) {
+            const uint32_t g = gt + t, buf = g & 1;
+            const int ks = kt % C::kKStages;
+            if (!mbar_wait(&s_free[buf], ((g >> 1) & 1) ^ 1, abort_flag) ||
+                !mbar_wait(&k_full[ks], (kt / C::kKStages) & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after_sync();
+            const uint32_t kb = aK + ks * C::kKBytes;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+              mma_f16_ss(tmem + buf * 128, make_smem_desc(aQ + off, 16, 1024, 2),
+                         make_smem_desc(kb + off, 16, 1024, 2), idesc_s, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(&k_empty[ks]);
+            mma_commit(&s_full[buf]);
+            ++kt;
+          }
+          if (t >= 1) {
+            const uint32_t g = gt + t - 1;
+            const int vs = vt % C::kVStages;
+            if (!mbar_wait(p_full, g & 1, abort_flag) ||
+                !mbar_wait(&v_full[vs], (vt / C::kVStages) & 1, abort_flag)) { ok = false; break; }
+            if (t == 1 && gi > 0 && !mbar_wait(o_free, (gi - 1) & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after_sync();
+            const uint32_t vb = aV + vs * C::kVBytes;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+              mma_f16_ss(tmem_o, make_smem_desc(aP + aoff, 16, 1024, 2),
+                         make_smem_desc(vb + kk * 2048, 16384, 1024, 2), idesc_o,
+                         (t > 1 || kk > 0) ? 1u : 0u);
+            }
+            mma_commit(&v_empty[vs]);
+            mma_commit(o_ready);
+            ++vt;
+          }
+        }
+        if (!ok) break;
+        mma_commit(q_empty);
+        gt += T;
+        ++gi;
+      }
+      if (gi > 0 || gt > 0) {
+        mma_commit(drain);
+        (void)mbar_wait(drain, 0, nullptr);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int half = r >> 6;
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    uint8_t* prow = sP + r * 128;
+    uint32_t gi = 0, gt = 0;
+    for (int64_t item = blockIdx.x; item < p.items; item += gridDim.x) {
+      const int T = p.ntiles[item];
+      const int bh = static_cast<int>(item / p.P), pr = static_cast<int>(item % p.P);
+      const int b = bh / p.Hq, h = bh % p.Hq;
+      const int row = 128 * pr + r;
+      const int64_t ooff = b * p.o_s0 + h * p.o_s1 + static_cast<int64_t>(row) * p.o_s2;
+      using OutT = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
+      OutT* orow = reinterpret_cast<OutT*>(p.out) + ooff;
+      if (T == 0) {
+        if (row < p.N) {
+#pragma unroll
+          for (int c = 0; c < D; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
+          if (p.lse) p.lse[static_cast<int64_t>(bh) * p.N + row] = -INFINITY;
+        }
+        continue;
+      }
+      const uint32_t* ul = p.ulist + item * p.stride;
+      float m_run = -INFINITY, l = 0.f;
+      bool ok = true;
+      for (int t = 0; t < T; ++t) {
+        const uint32_t g = gt + t, buf = g & 1;
+        const uint32_t e0 = ul[2 * t], e1 = ul[2 * t + 1];
+        int lim[2];
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const uint32_t e = x ? e1 : e0;
+          const int j = static_cast<int>(e & kIdxMask);
+          int n = ((e >> (30 + half)) & 1u) ? min(64, p.N - 64 * j) : 0;
+          if (p.causal) n = min(n, row - 64 * j + 1);
+          lim[x] = max(n, 0);
+        }
+        const bool okw = mbar_wait(&s_full[buf], (g >> 1) & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, okw)) { ok = false; break; }
+        tc_fence_after_sync();
+        uint32_t s[128];
+        tmem_ld32(tmem + lane_addr + buf * 128 + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+        tmem_ld32(tmem + lane_addr + buf * 128 + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+        tmem_ld32(tmem + lane_addr + buf * 128 + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
+        tmem_ld32(tmem + lane_addr + buf * 128 + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
+        tmem_wait_ld();
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[buf]);
+
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          const bool valid = (c < 64) ? (c < lim[0]) : (c - 64 < lim[1]);
+          if (valid) mx = fmaxf(mx, __uint_as_float(s[c]));
+        }
+        const float m_tile = mx * p.scale_log2;  // -inf stays -inf (scale > 0)
+        float alpha = 1.f;
+        bool need = false;
+        if (m_run == -INFINITY) {
+          m_run = m_tile;
+        } else if (m_tile > m_run + kRescaleThreshold) {
+          alpha = ex2(m_run - m_tile);
+          need = true;
+          m_run = m_tile;
+          l *= alpha;
+        }
+        const bool live = m_run != -INFINITY;
+        uint32_t pk[64];
+        float lsum = 0.f;
+#pragma unroll
+        for (int c = 0; c < 128; c += 2) {
+          const bool v0 = (c < 64) ? (c < lim[0]) : (c - 64 < lim[1]);
+          const bool v1 = (c + 1 < 64) ? (c + 1 < lim[0]) : (c + 1 - 64 < lim[1]);
+          const float p0 = (v0 && live) ? ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, -m_run)) : 0.f;
+          const float p1 = (v1 && live) ? ex2(fmaf(__uint_as_float(s[c + 1]), p.scale_log2, -m_run)) : 0.f;
+          lsum += p0 + p1;
+          if constexpr (kBF16) {
+            __nv_bfloat162 v2 = __floats2bfloat162_rn(p0, p1);
+            pk[c >> 1] = *reinterpret_cast<uint32_t*>(&v2);
+          } else {
+            __half2 v2 = __floats2half2_rn(p0, p1);
+            pk[c >> 1] = *reinterpret_cast<uint32_t*>(&v2);
+          }
+        }
+        l += lsum;
+
+        if (t > 0) {
+          const bool okp = mbar_wait(o_ready, (g - 1) & 1, abort_flag);
+          if (!__all_sync(0xffffffffu, okp)) { ok = false; break; }
+          tc_fence_after_sync();
+        }
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+          for (int c = 0; c < D; c += 32) {
+            uint32_t o[32];
+            tmem_ld32(tmem_o + lane_addr + c, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int x = 0; x < 32; ++x) o[x] = __float_as_uint(__uint_as_float(o[x]) * alpha);
+            tmem_st32(tmem_o + lane_addr + c, o);
+          }
+          tmem_wait_st();
+        }
+        // P row -> 128-byte-swizzled K-major tile (two 64-key atoms of 16 KB)
+#pragma unroll
+        for (int ch = 0; ch < 16; ++ch) {
+          const int atom = ch >> 3, cc = ch & 7;
+          uint4 v = make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+          *reinterpret_cast<uint4*>(prow + atom * 16384 + ((cc ^ (r & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
+      }
+      if (!ok) break;
+      // ---- epilogue: O / l
+      const uint32_t glast = gt + T - 1;
+      const bool oko = mbar_wait(o_ready, glast & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, oko)) break;
+      tc_fence_after_sync();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+      for (int c = 0; c < D; c += 32) {
+        uint32_t o[32];
+        tmem_ld32(tmem_o + lane_addr + c, o);
+        tmem_wait_ld();
+        if (row < p.N) {
+#pragma unroll
+          for (int x = 0; x < 32; x += 8) {
+            uint32_t w[4];
+#pragma unroll
+            for (int y = 0; y < 4; ++y) {
+              const float a0 = __uint_as_float(o[x + 2 * y]) * inv, a1 = __uint_as_float(o[x + 2 * y + 1]) * inv;
+              if constexpr (kBF16) {
+                __nv_bfloat162 v2 = __floats2bfloat162_rn(a0, a1);
+                w[y] = *reinterpret_cast<uint32_t*>(&v2);
+              } else {
+                __half2 v2 = __floats2half2_rn(a0, a1);
+                w[y] = *reinterpret_cast<uint32_t*>(&v2);
+              }
+            }
+            *reinterpret_cast<uint4*>(orow + c + x) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+      if (row < p.N && p.lse)
+        p.lse[static_cast<int64_t>(bh) * p.N + row] = l > 0.f ? (m_run + __log2f(l)) * kLn2 : -INFINITY;
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_free);
+      gt += T;
+      ++gi;
+    }
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ CUDA-core kernel
+struct SimtParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  const int32_t* kv_idx;
+  const int32_t* kv_num;
+  void* out;
+  float* lse;
+  int32_t Hq, Hkv, N, M, bs, D, kmax;
+  int64_t qs[3], ks[3], vs[3], os[3];
+  float scale;
+  int32_t causal;
+};
+
+template <typename T>
+__device__ __forceinline__ float ld_elem(const void* p, int64_t i) {
+  if constexpr (std::is_same<T, float>::value) return static_cast<const float*>(p)[i];
+  else if constexpr (std::is_same<T, __half>::value) return __half2float(static_cast<const __half*>(p)[i]);
+  else return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ void st_elem(void* p, int64_t i, float v) {
+  if constexpr (std::is_same<T, float>::value) static_cast<float*>(p)[i] = v;
+  else if constexpr (std::is_same<T, __half>::value) static_cast<__half*>(p)[i] = __float2half_rn(v);
+  else static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+}
+
+// grid (M, Hq, B), block 128 threads; thread t owns query row i*bs + t (t < bs).
+template <typename T>
+__global__ void __launch_bounds__(128) attn_simt_kernel(const SimtParams p) {
+  extern __shared__ float sm[];
+  const int D = p.D, bs = p.bs;
+  float* sk = sm;                  // [bs][D+1]
+  float* sv = sk + bs * (D + 1);   // [bs][D]
+  float* sq = sv + bs * D;         // [bs][D+1]
+  const int i = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.Hq / p.Hkv);
+  const int t = threadIdx.x;
+  const int row = i * bs + t;
+  for (int e = t; e < bs * D; e += blockDim.x) {
+    const int rr = e / D, d = e % D;
+    const int n = i * bs + rr;
+    sq[rr * (D + 1) + d] = n < p.N ? ld_elem<T>(p.q, b * p.qs[0] + h * p.qs[1] + n * p.qs[2] + d) : 0.f;
+  }
+  float o[128];
+#pragma unroll
+  for (int d = 0; d < 128; ++d) o[d] = 0.f;
+  float m = -INFINITY, l = 0.f;
+  const int64_t lrow = (static_cast<int64_t>(b) * p.Hq + h) * p.M + i;
+  const int nb = min(max(p.kv_num[lrow], 0), p.kmax);
+  for (int x = 0; x < nb; ++x) {
+    const int j = p.kv_idx[lrow * p.kmax + x];
+    __syncthreads();
+    if (j < 0 || j >= p.M) continue;
+    for (int e = t; e < bs * D; e += blockDim.x) {
+      const int rr = e / D, d = e % D;
+      const int n = j * bs + rr;
+      const bool in = n < p.N;
+      sk[rr * (D + 1) + d] = in ? ld_elem<T>(p.k, b * p.ks[0] + hk * p.ks[1] + n * p.ks[2] + d) : 0.f;
+      sv[rr * D + d] = in ? ld_elem<T>(p.v, b * p.vs[0] + hk * p.vs[1] + n * p.vs[2] + d) : 0.f;
+    }
+    __syncthreads();
+    if (t < bs && row < p.N) {
+      for (int kk = 0; kk < bs; ++kk) {
+        const int kp = j * bs + kk;
+        if (kp >= p.N || (p.causal && kp > row)) continue;
+        float s = 0.f;
+        for (int d = 0; d < D; ++d) s = fmaf(sq[t * (D + 1) + d], sk[kk * (D + 1) + d], s);
+        s *= p.scale;
+        const float mn = fmaxf(m, s);
+        const float corr = expf(m - mn);
+        const float pe = expf(s - mn);
+        l = l * corr + pe;
+#pragma unroll
+        for (int d = 0; d < 128; ++d)
+          if (d < D) o[d] = o[d] * corr + pe * sv[kk * D + d];
+        m = mn;
+      }
+    }
+  }
+  if (t < bs && row < p.N) {
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+    for (int d = 0; d < 128; ++d)
+      if (d < D) st_elem<T>(p.out, b * p.os[0] + h * p.os[1] + static_cast<int64_t>(row) * p.os[2] + d, o[d] * inv);
+    if (p.lse) p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.N + row] = l > 0.f ? m + logf(l) : -INFINITY;
+  }
+}
+
+struct WsLayout {
+  size_t ulist_off, ntiles_off, total;
+  int32_t stride;
+  int64_t items;
+};
+
+static WsLayout ws_layout(int64_t B, int64_t Hq, int64_t N, int64_t bs, int64_t kmax) {
+  WsLayout L{};
+  const int64_t M = (N + bs - 1) / bs;
+  const int64_t P = (M + 1) / 2;
+  L.items = B * Hq * P;
+  L.stride = static_cast<int32_t>(2 * kmax + 2);
+  L.ulist_off = 0;
+  const size_t ubytes = static_cast<size_t>(L.items) * L.stride * 4;
+  L.ntiles_off = (ubytes + 255) / 256 * 256;
+  L.total = L.ntiles_off + (static_cast<size_t>(L.items) * 4 + 255) / 256 * 256;
+  return L;
+}
+
+static bool use_tensor_cores(int dtype, int64_t D, int64_t bs) {
+  return (dtype == CAB_DTYPE_BF16 || dtype == CAB_DTYPE_F16) && bs == 64 && (D == 64 || D == 128);
+}
+
+template <int D, bool kBF16>
+static int launch_tc(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const Params& p,
+                     cudaStream_t st) {
+  auto kern = attn_tc_kernel<D, kBF16>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::kSmem);
+  const int grid = static_cast<int>(std::min<int64_t>(p.items, current_sm_count()));
+  kern<<<grid, 192, Cfg<D>::kSmem, st>>>(qm, km, vm, p);
+  return check_launch("attn_tc_kernel");
+}
+
+}  // namespace attn
+}  // namespace cab
+
+using namespace cab;
+
+extern "C" int cab_sparse_attn_workspace_size(int64_t B, int64_t Hq, int64_t N, int64_t D, int64_t block_size,
+                                              int64_t kmax, int dtype, size_t* bytes) {
+  if (!bytes) return fail(CAB_ERR_INVALID_ARG, "attn_workspace_size: NULL output");
+  if (B <= 0 || Hq <= 0 || N <= 0 || block_size <= 0 || kmax <= 0)
+    return fail(CAB_ERR_INVALID_ARG, "attn_workspace_size: non-positive size");
+  *bytes = attn::use_tensor_cores(dtype, D, block_size) ? attn::ws_layout(B, Hq, N, block_size, kmax).total : 0;
+  return CAB_OK;
+}
+
+extern "C" int cab_sparse_attn_fwd(const void* q, const void* k, const void* v, const int32_t* kv_idx,
+                                   const int32_t* kv_num, void* out, float* lse, int64_t B, int64_t Hq,
+                                   int64_t Hkv, int64_t N, int64_t D, int64_t block_size, int64_t kmax,
+                                   const int64_t* q_strides, const int64_t* k_strides,
+                                   const int64_t* v_strides, const int64_t* o_strides, float softmax_scale,
+                                   int causal, int dtype, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+  using namespace attn;
+  if (!q || !k || !v || !kv_idx || !kv_num || !out) return fail(CAB_ERR_INVALID_ARG, "attn: NULL pointer");
+  if (!q_strides || !k_strides || !v_strides || !o_strides) return fail(CAB_ERR_INVALID_ARG, "attn: NULL strides");
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || N <= 0 || D <= 0 || block_size <= 0 || kmax <= 0)
+    return fail(CAB_ERR_INVALID_ARG, "attn: non-positive size");
+  if (Hq % Hkv != 0) return fail(CAB_ERR_INVALID_ARG, "attn: Hq %% Hkv != 0");
+  if (!(softmax_scale > 0.f)) return fail(CAB_ERR_INVALID_ARG, "attn: softmax_scale must be > 0");
+  const size_t es = dtype_size(dtype);
+  if (!es) return fail(CAB_ERR_UNSUPPORTED, "attn: unknown dtype %d", dtype);
+  if (N >= (int64_t)1 << 31 || B * Hq >= (int64_t)1 << 31) return fail(CAB_ERR_UNSUPPORTED, "attn: sizes exceed int32");
+  const int64_t M = (N + block_size - 1) / block_size;
+  if (M >= (int64_t)1 << 30) return fail(CAB_ERR_UNSUPPORTED, "attn: too many blocks");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  if (use_tensor_cores(dtype, D, block_size)) {
+    const WsLayout L = ws_layout(B, Hq, N, block_size, kmax);
+    if (!workspace || workspace_bytes < L.total)
+      return fail(CAB_ERR_WORKSPACE, "attn: workspace of %zu bytes needed, %zu given", L.total, workspace_bytes);
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(workspace))
+      return fail(CAB_ERR_INVALID_ARG, "attn: pointers must be 16-byte aligned");
+    const int64_t* ss[4] = {q_strides, k_strides, v_strides, o_strides};
+    for (int x = 0; x < 4; ++x)
+      for (int i = 0; i < 3; ++i)
+        if (ss[x][i] <= 0 || (ss[x][i] * static_cast<int64_t>(es)) % 16 != 0)
+          return fail(CAB_ERR_INVALID_ARG, "attn: strides must be positive multiples of 16 bytes");
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    UnionParams up{};
+    up.kv_idx = kv_idx;
+    up.kv_num = kv_num;
+    up.ulist = reinterpret_cast<uint32_t*>(ws + L.ulist_off);
+    up.ntiles = reinterpret_cast<int32_t*>(ws + L.ntiles_off);
+    up.items = L.items;
+    up.M = static_cast<int32_t>(M);
+    up.P = static_cast<int32_t>((M + 1) / 2);
+    up.kmax = static_cast<int32_t>(kmax);
+    up.stride = L.stride;
+    up.words = static_cast<int32_t>((M + 31) / 32);
+    const size_t usmem = static_cast<size_t>(4) * 2 * up.words * 4;
+    if (usmem > 200 * 1024) return fail(CAB_ERR_UNSUPPORTED, "attn: M too large for the union kernel");
+    cudaFuncSetAttribute(pair_union_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)usmem);
+    const int ugrid = static_cast<int>(std::min<int64_t>((L.items + 3) / 4, (int64_t)current_sm_count() * 16));
+    pair_union_kernel<<<ugrid, 128, usmem, st>>>(up);
+    if (int rc = check_launch("pair_union_kernel")) return rc;
+
+    CUtensorMap qm{}, km{}, vm{};
+    auto mk = [&](CUtensorMap* m, const void* ptr, int64_t H, const int64_t* s, uint32_t rows) {
+      uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(N), static_cast<uint64_t>(H), static_cast<uint64_t>(B)};
+      uint64_t str[3] = {static_cast<uint64_t>(s[2]) * es, static_cast<uint64_t>(s[1]) * es, static_cast<uint64_t>(s[0]) * es};
+      uint32_t box[4] = {64, rows, 1, 1};
+      return make_tensor_map(m, tma_type(dtype), 4, ptr, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    };
+    if (int rc = mk(&qm, q, Hq, q_strides, 128)) return rc;
+    if (int rc = mk(&km, k, Hkv, k_strides, 64)) return rc;
+    if (int rc = mk(&vm, v, Hkv, v_strides, 64)) return rc;
+    Params p{};
+    p.B = static_cast<int32_t>(B);
+    p.Hq = static_cast<int32_t>(Hq);
+    p.Hkv = static_cast<int32_t>(Hkv);
+    p.N = static_cast<int32_t>(N);
+    p.M = static_cast<int32_t>(M);
+    p.P = up.P;
+    p.items = L.items;
+    p.o_s0 = o_strides[0];
+    p.o_s1 = o_strides[1];
+    p.o_s2 = o_strides[2];
+    p.out = out;
+    p.lse = lse;
+    p.ulist = up.ulist;
+    p.ntiles = up.ntiles;
+    p.stride = L.stride;
+    p.scale_log2 = softmax_scale * kLog2e;
+    p.causal = causal != 0;
+    const bool bf = dtype == CAB_DTYPE_BF16;
+    if (D == 128) return bf ? launch_tc<128, true>(qm, km, vm, p, st) : launch_tc<128, false>(qm, km, vm, p, st);
+    return bf ? launch_tc<64, true>(qm, km, vm, p, st) : launch_tc<64, false>(qm, km, vm, p, st);
+  }
+
+  if (block_size > 128 || D > 128)
+    return fail(CAB_ERR_UNSUPPORTED, "attn: CUDA-core path needs block_size <= 128 and D <= 128");
+  SimtParams sp{};
+  sp.q = q; sp.k = k; sp.v = v; sp.kv_idx = kv_idx; sp.kv_num = kv_num; sp.out = out; sp.lse = lse;
+  sp.Hq = static_cast<int32_t>(Hq); sp.Hkv = static_cast<int32_t>(Hkv); sp.N = static_cast<int32_t>(N);
+  sp.M = static_cast<int32_t>(M); sp.bs = static_cast<int32_t>(block_size); sp.D = static_cast<int32_t>(D);
+  sp.kmax = static_cast<int32_t>(kmax);
+  for (int i = 0; i < 3; ++i) {
+    sp.qs[i] = q_strides[i]; sp.ks[i] = k_strides[i]; sp.vs[i] = v_strides[i]; sp.os[i] = o_strides[i];
+  }
+  sp.scale = softmax_scale;
+  sp.causal = causal != 0;
+  const size_t smem = static_cast<size_t>(block_size) * (3 * D + 2) * sizeof(float);
+  dim3 grid(static_cast<unsigned>(M), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
+  switch (dtype) {
+    case CAB_DTYPE_F32:
+      cudaFuncSetAttribute(attn_simt_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attn_simt_kernel<float><<<grid, 128, smem, st>>>(sp);
+      break;
+    case CAB_DTYPE_F16:
+      cudaFuncSetAttribute(attn_simt_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attn_simt_kernel<__half><<<grid, 128, smem, st>>>(sp);
+      break;
+    default:
+      cudaFuncSetAttribute(attn_simt_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attn_simt_kernel<__nv_bfloat16><<<grid, 128, smem, st>>>(sp);
+      break;
+  }
+  return check_launch("attn_simt_kernel");
+}

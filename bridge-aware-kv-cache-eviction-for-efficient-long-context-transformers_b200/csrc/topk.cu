@@ -1,0 +1,199 @@
+// K3: per-row top-k block selection (HBM-bound on reading the score matrix).
+//
+// One warp owns one row (b, h, i) of the [BH, M, M] score matrix at a time. It reads the
+// row once (coalesced, 16-byte loads when M % 4 == 0) and stores it in shared memory as
+// order-preserving 32-bit keys: the preferred direction (select_high or not) maps to
+// "larger key", NaN to the least preferred real key, -0 to +0, excluded (causal j > i)
+// candidates to 0 and the forced diagonal to 0xFFFFFFFF. A four-pass MSB-first radix
+// select (256-bin shared-memory histogram, warp-aggregated atomics) finds the k_i-th
+// largest key tau. A final pass in index order takes every key > tau and the lowest-index
+// keys == tau until k_i are taken, compacting with ballots so kv_idx comes out ascending,
+// and writes the dense 0/1 mask of the row.
+//
+// Selection rule: per-(b,h,row) top-k of the Forman-Ricci score (generate_block_mask,
+// called with select_high / keep_diagonal / causal at experiments/longbench_qa/
+// methods.py:339-345; k = max(1, int((1 - sparsity) * M)) as at methods.py:252).
+
+#include "cab_host.h"
+#include "cab_ptx.cuh"
+
+#include <algorithm>
+
+namespace cab {
+namespace topk {
+
+struct Params {
+  const float* scores;
+  int32_t* kv_idx;
+  int32_t* kv_num;
+  uint8_t* dense;
+  int64_t rows;  // BH * M
+  int32_t M, k;
+  int32_t select_high, keep_diagonal, causal;
+  int32_t warps;
+};
+
+__device__ __forceinline__ uint32_t to_key(float f, bool high) {
+  float g = high ? f : -f;
+  if (g != g) g = -__int_as_float(0x7f800000);  // NaN -> -inf (least preferred)
+  if (g == 0.0f) g = 0.0f;                       // -0 -> +0
+  const uint32_t bits = __float_as_uint(g);
+  return (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(256) topk_kernel(const Params p) {
+  extern __shared__ __align__(16) uint32_t smem[];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int M = p.M;
+  const int row_words = (M + 3) & ~3;
+  uint32_t* keys = smem + static_cast<size_t>(warp) * (row_words + 256);
+  uint32_t* hist = keys + row_words;
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  const bool high = p.select_high != 0;
+
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * p.warps + warp; row < p.rows;
+       row += static_cast<int64_t>(gridDim.x) * p.warps) {
+    const int i = static_cast<int>(row % M);
+    const int ncand = p.causal ? i + 1 : M;
+    const int kk = min(p.k, ncand);
+    const float* src = p.scores + row * M;
+
+    // ---- load the row as keys
+    if ((M & 3) == 0) {
+      const float4* src4 = reinterpret_cast<const float4*>(src);
+      for (int j4 = lane; j4 < (M >> 2); j4 += 32) {
+        const float4 v = __ldg(src4 + j4);
+        const float vals[4] = {v.x, v.y, v.z, v.w};
+        uint4 kv;
+        uint32_t* kp = &kv.x;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int j = 4 * j4 + t;
+          uint32_t key = to_key(vals[t], high);
+          if (j >= ncand) key = 0u;
+          if (p.keep_diagonal && j == i) key = 0xFFFFFFFFu;
+          kp[t] = key;
+        }
+        reinterpret_cast<uint4*>(keys)[j4] = kv;
+      }
+    } else {
+      for (int j = lane; j < M; j += 32) {
+        uint32_t key = to_key(__ldg(src + j), high);
+        if (j >= ncand) key = 0u;
+        if (p.keep_diagonal && j == i) key = 0xFFFFFFFFu;
+        keys[j] = key;
+      }
+    }
+    __syncwarp();
+
+    // ---- radix select of the kk-th largest key
+    uint32_t prefix = 0u, pmask = 0u;
+    int remaining = kk;
+#pragma unroll 1
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int b = lane; b < 256; b += 32) hist[b] = 0u;
+      __syncwarp();
+      for (int base = 0; base < M; base += 32) {
+        const int j = base + lane;
+        const uint32_t key = j < M ? keys[j] : 0u;
+        const bool match = j < M && (key & pmask) == prefix;
+        const uint32_t digit = match ? ((key >> shift) & 255u) : 0x100u;
+        const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+        if (match && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
+      }
+      __syncwarp();
+      // lane l owns bins 255-8l .. 248-8l (highest bins first)
+      uint32_t c[8];
+      uint32_t tot = 0;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        c[t] = hist[255 - 8 * lane - t];
+        tot += c[t];
+      }
+      uint32_t incl = tot;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t o = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += o;
+      }
+      uint32_t running = incl - tot;
+      int found_digit = -1;
+      uint32_t found_above = 0;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        if (found_digit < 0 && running < static_cast<uint32_t>(remaining) &&
+            running + c[t] >= static_cast<uint32_t>(remaining)) {
+          found_digit = 255 - 8 * lane - t;
+          found_above = running;
+        }
+        running += c[t];
+      }
+      const uint32_t who = __ballot_sync(0xffffffffu, found_digit >= 0);
+      const int src_lane = __ffs(who) - 1;
+      const int digit = __shfl_sync(0xffffffffu, found_digit, src_lane);
+      const uint32_t above = __shfl_sync(0xffffffffu, found_above, src_lane);
+      prefix |= static_cast<uint32_t>(digit) << shift;
+      pmask |= 255u << shift;
+      remaining -= static_cast<int>(above);
+      __syncwarp();
+    }
+    const uint32_t tau = prefix;
+    const int take_eq = remaining;  // keys == tau to take, lowest index first
+
+    // ---- select in index order, compact, write outputs
+    int32_t* out_idx = p.kv_idx + row * p.k;
+    uint8_t* out_dense = p.dense ? p.dense + row * M : nullptr;
+    int eq_seen = 0, taken = 0;
+    for (int base = 0; base < M; base += 32) {
+      const int j = base + lane;
+      const uint32_t key = j < M ? keys[j] : 0u;
+      const bool gt = j < M && key > tau;
+      const bool eq = j < M && key == tau;
+      const uint32_t eq_bits = __ballot_sync(0xffffffffu, eq);
+      const int eq_rank = eq_seen + __popc(eq_bits & lt_mask);
+      const bool take = gt || (eq && eq_rank < take_eq);
+      eq_seen += __popc(eq_bits);
+      const uint32_t take_bits = __ballot_sync(0xffffffffu, take);
+      if (take) out_idx[taken + __popc(take_bits & lt_mask)] = j;
+      taken += __popc(take_bits);
+      if (out_dense && j < M) out_dense[j] = take ? 1 : 0;
+    }
+    for (int pos = kk + lane; pos < p.k; pos += 32) out_idx[pos] = -1;
+    if (lane == 0) p.kv_num[row] = kk;
+    __syncwarp();
+  }
+}
+
+}  // namespace topk
+}  // namespace cab
+
+using namespace cab;
+
+extern "C" int cab_topk_blocks(const float* scores, int32_t* kv_idx, int32_t* kv_num,
+                               uint8_t* dense_mask, int64_t BH, int64_t M, int64_t k,
+                               int select_high, int keep_diagonal, int causal, void* stream) {
+  if (!scores || !kv_idx || !kv_num) return fail(CAB_ERR_INVALID_ARG, "topk: NULL pointer");
+  if (BH <= 0 || M <= 0) return fail(CAB_ERR_INVALID_ARG, "topk: non-positive size");
+  if (k < 1 || k > M) return fail(CAB_ERR_INVALID_ARG, "topk: k=%lld outside [1, M=%lld]", (long long)k, (long long)M);
+  if (M > 49152) return fail(CAB_ERR_UNSUPPORTED, "topk: M=%lld > 49152", (long long)M);
+  topk::Params p{};
+  p.scores = scores; p.kv_idx = kv_idx; p.kv_num = kv_num; p.dense = dense_mask;
+  p.rows = BH * M;
+  p.M = static_cast<int32_t>(M);
+  p.k = static_cast<int32_t>(k);
+  p.select_high = select_high != 0;
+  p.keep_diagonal = keep_diagonal != 0;
+  p.causal = causal != 0;
+  const size_t per_warp = (static_cast<size_t>((M + 3) & ~3) + 256) * sizeof(uint32_t);
+  int warps = static_cast<int>(std::min<size_t>(8, (200 * 1024) / per_warp));
+  if (warps < 1) warps = 1;
+  p.warps = warps;
+  const size_t smem = per_warp * warps;
+  const int64_t ctas_needed = (p.rows + warps - 1) / warps;
+  const int per_sm = std::max<int>(1, static_cast<int>((227 * 1024) / (smem + 1024)));
+  const int grid = static_cast<int>(std::min<int64_t>(ctas_needed, (int64_t)current_sm_count() * per_sm));
+  cudaFuncSetAttribute(topk::topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  topk::topk_kernel<<<grid, 32 * warps, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_launch("topk_kernel");
+}

@@ -1,0 +1,171 @@
+/*
+ * cab_capi.h -- C ABI of libcab_b200.so, the sm_100a kernels of CAB-Attention's prefill
+ * path (Max-L2 coarsening -> coarse Forman-Ricci score -> per-row top-k block mask ->
+ * block-sparse attention).
+ *
+ * Conventions shared by every entry point:
+ *  - Plain device pointers and sizes; no framework types. Outputs and scratch memory are
+ *    allocated by the caller. Entry points that need scratch memory have a
+ *    `*_workspace_size` query.
+ *  - Every call is ordered on the caller's `stream` (a cudaStream_t passed as void*),
+ *    does not synchronise with the host and keeps no state between calls.
+ *  - Return value: CAB_OK or a CAB_ERR_* code; cab_last_error_string() (per host thread)
+ *    describes the last failure. Nothing falls back to another implementation.
+ *  - Tensors are row-major. "[B,H,N,D] with strides" means element (b,h,n,d) lives at
+ *    ptr[b*s[0] + h*s[1] + n*s[2] + d] (strides in elements, innermost dimension dense).
+ *  - dtype: CAB_DTYPE_BF16 / CAB_DTYPE_F16 run on the tensor cores (tcgen05); CAB_DTYPE_F32
+ *    runs on CUDA cores in fp32 / fp64.
+ *
+ * The reference (Js-Hwang1/Bridge-Aware-KV-Cache-Eviction-for-Efficient-Long-Context-
+ * Transformers) implements this path in Python modules listed in README.md:189-196
+ * (cab_attention/kernels/coarsening.py, cab_attention/kernels/frc_kernel.py,
+ * cab_attention/coarse_predictor.py, cab_attention/cab_attention.py); the snapshot keeps
+ * their callers, cited per entry point below.
+ */
+#ifndef CAB_CAPI_H_
+#define CAB_CAPI_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CAB_API_VERSION 1
+
+#if defined(__GNUC__)
+#define CAB_API __attribute__((visibility("default")))
+#else
+#define CAB_API
+#endif
+
+/* status codes */
+#define CAB_OK 0
+#define CAB_ERR_INVALID_ARG 1 /* null pointer, bad size, misaligned pointer or stride */
+#define CAB_ERR_UNSUPPORTED 2 /* dtype / shape / device not handled by the kernels     */
+#define CAB_ERR_LAUNCH 3      /* CUDA launch or driver error                           */
+#define CAB_ERR_TIMEOUT 4     /* a device-side wait gave up (see cab_device_status)     */
+#define CAB_ERR_WORKSPACE 5   /* workspace missing or smaller than *_workspace_size     */
+
+/* element types */
+#define CAB_DTYPE_F32 0
+#define CAB_DTYPE_F16 1
+#define CAB_DTYPE_BF16 2
+
+/* Direct-connection normalisation of the affinity (compute_block_frc `normalization`) */
+#define CAB_NORM_ABS 0    /* |A|                                      */
+#define CAB_NORM_MINMAX 1 /* (A - min) / (max - min + 1e-8) per (b,h) */
+#define CAB_NORM_RAW 2    /* A                                        */
+
+/* FRC formula (compute_block_frc `formula`) */
+#define CAB_FORMULA_ADDITIVE 0       /* F = Direct - lambda * T                        */
+#define CAB_FORMULA_MULTIPLICATIVE 1 /* F = Direct / (1 + lambda * T / (Direct + 1e-8)) */
+
+/* redundancy scaling */
+#define CAB_RED_SCALE_NONE 0  /* T = Direct @ Direct       */
+#define CAB_RED_SCALE_INV_M 1 /* T = (Direct @ Direct) / M */
+
+/* Library version (CAB_API_VERSION). */
+CAB_API int cab_get_version(void);
+
+/* Text of the last error raised on this host thread ("" if none). */
+CAB_API const char* cab_last_error_string(void);
+
+/* 1 if `device` is an sm_100 part these kernels were built for, else 0. */
+CAB_API int cab_device_supported(int device);
+
+/* Synchronises `stream`, then stores and clears the device-side status word of the
+ * current device (0 = fine, CAB_ERR_TIMEOUT if a kernel's bounded wait gave up). */
+CAB_API int cab_device_status(void* stream, int* status);
+
+/*
+ * Max-L2 coarsening: for every `block_size`-token block of q [B,Hq,N,D] and
+ * k [B,Hkv,N,D], pick the token with the largest L2 norm (norm^2 accumulated in fp64;
+ * the lowest index wins ties; a partial last block uses its valid tokens) and copy it to
+ * q_coarse [B,Hq,M,D] / k_coarse [B,Hkv,M,D] (dense), M = ceil(N / block_size).
+ * q_idx / k_idx ([B,Hq,M] / [B,Hkv,M] int32, absolute token index) may be NULL.
+ * Either side may be skipped by passing NULL for its input and outputs.
+ * Strides: q_strides/k_strides = {b, h, n} in elements; base pointers and n-strides must be
+ * 16-byte aligned. D * sizeof(dtype) must be a multiple of 16 and <= 1024 bytes.
+ * Replaces coarsen_qk_max_l2 / coarsen_qk_max_l2_pytorch (cab_attention/kernels/
+ * coarsening.py; callers benchmarks/kernel_benchmark.py:82-85,
+ * benchmarks/quick_kernel_test.py:54-57, experiments/longbench_qa/methods.py:303,327).
+ */
+CAB_API int cab_coarsen_maxl2(const void* q, const void* k, void* q_coarse, void* k_coarse,
+                      int32_t* q_idx, int32_t* k_idx, int64_t B, int64_t Hq, int64_t Hkv,
+                      int64_t N, int64_t D, int64_t block_size, const int64_t* q_strides,
+                      const int64_t* k_strides, int dtype, void* stream);
+
+/* Scratch bytes cab_frc needs for these sizes. */
+CAB_API int cab_frc_workspace_size(int64_t B, int64_t Hq, int64_t M, int64_t D, int dtype,
+                           int normalization, size_t* bytes);
+
+/*
+ * Coarse Forman-Ricci score per (b, query head):
+ *   A = q_coarse @ k_coarse^T / sqrt(D) / temperature      (query head h uses KV head
+ *                                                             h / (Hq / Hkv))
+ *   Direct = normalisation(A); T = Direct @ Direct (optionally / M)
+ *   F = formula(Direct, T, lambda_redundancy)
+ * q_coarse [B,Hq,M,D], k_coarse [B,Hkv,M,D] dense. Outputs [B,Hq,M,M] fp32 dense:
+ * frc (required), affinity (= Direct, may be NULL), redundancy (= T, may be NULL).
+ * bf16/f16: both products on tcgen05 tensor cores; T takes f16 operands (Direct rounded
+ * to f16, |Direct| must stay below 65504) with f32 accumulation. f32: A in fp32 on CUDA
+ * cores, T from an f16 hi/lo split (three tensor-core products).
+ * Replaces compute_block_frc (cab_attention/kernels/frc_kernel.py; callers
+ * experiments/longbench_qa/methods.py:330-336,384-389,452-458,
+ * benchmarks/kernel_benchmark.py:149,253, benchmarks/quick_kernel_test.py:67).
+ */
+CAB_API int cab_frc(const void* q_coarse, const void* k_coarse, float* frc, float* affinity,
+            float* redundancy, int64_t B, int64_t Hq, int64_t Hkv, int64_t M, int64_t D,
+            int dtype, float temperature, float lambda_redundancy, int normalization,
+            int formula, int redundancy_scale, void* workspace, size_t workspace_bytes,
+            void* stream);
+
+/*
+ * Per-row top-k block selection over scores [BH,M,M] fp32 (dense).
+ * Row i keeps k_i = min(k, #candidates) blocks: candidates are all j (or j <= i when
+ * `causal`); with `keep_diagonal` block i is always kept and the rest come from j != i.
+ * Preference: larger score if select_high else smaller; NaN least preferred; -0 == +0;
+ * ties go to the lower block index. Outputs: kv_idx [BH,M,k] int32 ascending, -1 padded;
+ * kv_num [BH,M] int32 (= k_i); dense_mask [BH,M,M] uint8 0/1 (may be NULL).
+ * Requires 1 <= k <= M <= 49152.
+ * Replaces generate_block_mask (cab_attention/kernels/frc_kernel.py; callers
+ * experiments/longbench_qa/methods.py:339-345,392-398, benchmarks/kernel_benchmark.py:197).
+ */
+CAB_API int cab_topk_blocks(const float* scores, int32_t* kv_idx, int32_t* kv_num, uint8_t* dense_mask,
+                    int64_t BH, int64_t M, int64_t k, int select_high, int keep_diagonal,
+                    int causal, void* stream);
+
+/* Scratch bytes cab_sparse_attn_fwd needs for these sizes. */
+CAB_API int cab_sparse_attn_workspace_size(int64_t B, int64_t Hq, int64_t N, int64_t D,
+                                   int64_t block_size, int64_t kmax, int dtype, size_t* bytes);
+
+/*
+ * Block-sparse attention forward: for each query block i of (b, h) attend to the key
+ * blocks kv_idx[b,h,i,0:kv_num[b,h,i]] of KV head h / (Hq / Hkv):
+ *   out = softmax(q k^T * softmax_scale + mask) v, mask = -inf outside the kept blocks,
+ *   beyond N, and (if `causal`) where key position > query position.
+ * A row that sees no key gets out = 0 and lse = -inf.
+ * q/out [B,Hq,N,D], k/v [B,Hkv,N,D] with {b,h,n} strides (elements, 16-byte aligned);
+ * kv_idx [B,Hq,M,kmax] int32 (ascending, entries < M), kv_num [B,Hq,M] int32;
+ * lse [B,Hq,N] fp32 natural-log sum-exp (may be NULL).
+ * bf16/f16 with block_size 64 and D in {64,128}: TMA-fed tcgen05 kernel, fp32 softmax
+ * and accumulation. Other cases (and f32): CUDA-core kernel, fp32 arithmetic.
+ * Replaces the FlexAttention / manual sparse-attention step of CABAttention.forward
+ * (cab_attention/cab_attention.py; README.md:44-46; manual path
+ * experiments/longbench_qa/methods.py:103-119,348-356).
+ */
+CAB_API int cab_sparse_attn_fwd(const void* q, const void* k, const void* v, const int32_t* kv_idx,
+                        const int32_t* kv_num, void* out, float* lse, int64_t B, int64_t Hq,
+                        int64_t Hkv, int64_t N, int64_t D, int64_t block_size, int64_t kmax,
+                        const int64_t* q_strides, const int64_t* k_strides,
+                        const int64_t* v_strides, const int64_t* o_strides,
+                        float softmax_scale, int causal, int dtype, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CAB_CAPI_H_ */
