@@ -16,6 +16,7 @@ import torch
 _LIB_NAME = "libcab_b200.so"
 _lock = threading.Lock()
 _lib = None
+_supported: dict = {}
 
 CAB_OK = 0
 CAB_ERR_TIMEOUT = 4
@@ -107,8 +108,11 @@ def require_cuda(*tensors: torch.Tensor) -> None:
             raise RuntimeError("CAB kernels run on an sm_100 CUDA device only (tensor on "
                                f"{t.device}); there is no CPU implementation")
     dev = next(t for t in tensors if t is not None).device
-    if not lib().cab_device_supported(dev.index if dev.index is not None else
-                                      torch.cuda.current_device()):
+    index = dev.index if dev.index is not None else torch.cuda.current_device()
+    ok = _supported.get(index)
+    if ok is None:
+        ok = _supported[index] = bool(lib().cab_device_supported(index))
+    if not ok:
         raise RuntimeError("CAB kernels are built for sm_100 (B200); device "
                            f"{torch.cuda.get_device_name(dev)} is not supported")
 

@@ -14,12 +14,13 @@ extern "C" int cab_get_version(void) { return CAB_API_VERSION; }
 extern "C" const char* cab_last_error_string(void) { return cab::last_error().c_str(); }
 
 extern "C" int cab_device_supported(int device) {
-  cudaDeviceProp prop;
-  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) {
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess) {
     cudaGetLastError();
     return 0;
   }
-  return (prop.major == 10 && prop.minor == 0) ? 1 : 0;
+  return (major == 10 && minor == 0) ? 1 : 0;
 }
 
 extern "C" int cab_device_status(void* stream, int* status) {
