@@ -1,0 +1,88 @@
+"""(batch x head) sharding on CPU ranks (gloo, world size 2): every unit is covered once,
+shards built from per-(b,h) seeds equal slices of the whole batch, and the per-rank oracle
+results gathered over the process group equal the single-process result."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from cab_attention import sharding, synthetic
+
+
+def test_unit_ranges_cover_everything_once():
+    for units in (1, 7, 16, 32, 33):
+        for world in (1, 2, 3, 4, 8):
+            got = []
+            for r in range(world):
+                s, e = sharding.unit_range(units, world, r)
+                got.extend(range(s, e))
+            assert got == list(range(units))
+
+
+def test_units_to_slices():
+    assert sharding.units_to_slices(3, 11, 4) == [(0, 3, 4), (1, 0, 4), (2, 0, 3)]
+    assert sharding.units_to_slices(0, 8, 8) == [(0, 0, 8)]
+
+
+def test_shard_inputs_equal_whole_batch_slices():
+    q, k, v = synthetic.make_qkv(4, 2, 2, 128, 16, torch.float32, seed=5)
+    q2, k2, v2 = synthetic.make_qkv(2, 2, 2, 128, 16, torch.float32, seed=5, batch_offset=2)
+    assert torch.equal(q[2:], q2) and torch.equal(k[2:], k2) and torch.equal(v[2:], v2)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, result_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import cab_oracle as orc
+        B, H, N, D, bs = 2, 3, 512, 16, 64
+        units = B * H
+        s, e = sharding.unit_range(units, world, rank)
+        q, k, v = synthetic.make_qkv(B, H, H, N, D, torch.float32, seed=9)
+        qs = q.reshape(units, 1, N, D)[s:e].permute(1, 0, 2, 3).numpy()
+        ks = k.reshape(units, 1, N, D)[s:e].permute(1, 0, 2, 3).numpy()
+        vs = v.reshape(units, 1, N, D)[s:e].permute(1, 0, 2, 3).numpy()
+        o = orc.predictor(qs, ks, bs, 0.75, 0.5)
+        out, _ = orc.block_sparse_attention(qs, ks, vs, o["kv_idx"], o["kv_num"], bs)
+        local = torch.from_numpy(out[0])                       # [units_local, N, D]
+        full = sharding.gather_units(local, units)
+        result_q.put((rank, full.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_sharded_oracle_layer_equals_single_process():
+    from oracle import cab_oracle as orc
+    world = 2
+    ctx = mp.get_context("spawn")
+    result_q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, result_q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(result_q.get(timeout=240) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    B, H, N, D, bs = 2, 3, 512, 16, 64
+    q, k, v = synthetic.make_qkv(B, H, H, N, D, torch.float32, seed=9)
+    o = orc.predictor(q.numpy(), k.numpy(), bs, 0.75, 0.5)
+    want, _ = orc.block_sparse_attention(q.numpy(), k.numpy(), v.numpy(), o["kv_idx"],
+                                         o["kv_num"], bs)
+    want = want.reshape(B * H, N, D)
+    for r in range(world):
+        np.testing.assert_allclose(results[r], want, rtol=1e-12, atol=1e-12)
