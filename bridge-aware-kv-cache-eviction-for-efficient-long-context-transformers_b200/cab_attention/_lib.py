@@ -51,6 +51,9 @@ SIGNATURES = {
     "cab_sparse_attn_fwd": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64,
                             _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_ptr, _c_ptr,
                             _c_ptr, _c_ptr, _c_float, _c_int, _c_int, _c_ptr, _c_size, _c_ptr],
+    "cab_sparse_attn_fwd_noalloc": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64,
+                                    _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_ptr,
+                                    _c_ptr, _c_ptr, _c_ptr, _c_float, _c_int, _c_int, _c_ptr],
 }
 
 

@@ -8,6 +8,7 @@
 #include "frc.cu"
 #include "topk.cu"
 #include "sparse_attn.cu"
+#include "noalloc.cu"
 
 extern "C" int cab_get_version(void) { return CAB_API_VERSION; }
 

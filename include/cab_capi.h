@@ -164,6 +164,28 @@ CAB_API int cab_sparse_attn_fwd(const void* q, const void* k, const void* v, con
                         float softmax_scale, int causal, int dtype, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/*
+ * cab_sparse_attn_fwd for callers that cannot allocate device memory: the same inputs,
+ * outputs and semantics, without the workspace arguments. No counterpart in the
+ * reference (an addition of this library).
+ * Who needs it: hosts whose device memory belongs to another allocator (a framework's
+ * caching allocator, a serving engine's pre-reserved pool) or bindings that link no CUDA
+ * allocator, so they cannot cudaMalloc the workspace cab_sparse_attn_fwd asks for.
+ * Scratch: a static 16 MiB device buffer inside the library, held on every GPU that loads
+ * it until the process exits. Sizes whose cab_sparse_attn_workspace_size exceeds 16 MiB
+ * return CAB_ERR_UNSUPPORTED. The first call on each device looks up the buffer's address
+ * (cudaGetSymbolAddress, with that device current); make that first call before any
+ * stream capture. All calls share the buffer, so calls that overlap on the GPU race.
+ * The call itself allocates nothing.
+ */
+CAB_API int cab_sparse_attn_fwd_noalloc(const void* q, const void* k, const void* v,
+                                        const int32_t* kv_idx, const int32_t* kv_num, void* out,
+                                        float* lse, int64_t B, int64_t Hq, int64_t Hkv, int64_t N,
+                                        int64_t D, int64_t block_size, int64_t kmax,
+                                        const int64_t* q_strides, const int64_t* k_strides,
+                                        const int64_t* v_strides, const int64_t* o_strides,
+                                        float softmax_scale, int causal, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
