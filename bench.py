@@ -373,8 +373,17 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-baseline-seconds", type=float, default=15.0)
     ap.add_argument("--reference-step-seconds", type=float, default=4.0)
+    ap.add_argument("--batch", type=int, default=None, help="override B per rank (profiling)")
+    ap.add_argument("--heads", type=int, default=None,
+                    help="override the KV-head count per rank, query heads scaled (profiling)")
     args = ap.parse_args()
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.batch is not None or args.heads is not None:
+        G = cfg["Hq"] // cfg["Hkv"]
+        cfg["B"] = args.batch if args.batch is not None else cfg["B"]
+        cfg["Hkv"] = args.heads if args.heads is not None else cfg["Hkv"]
+        cfg["Hq"] = cfg["Hkv"] * G
+        cfg["workload"] += f" [reduced to B={cfg['B']} Hq={cfg['Hq']} Hkv={cfg['Hkv']}]"
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
