@@ -33,6 +33,8 @@ extern "C" int cab_device_status(void* stream, int* status) {
   e = cudaMemcpyFromSymbol(&value, cab::g_device_status, sizeof(int));
   if (e == cudaSuccess) e = cudaMemcpyToSymbol(cab::g_device_status, &zero, sizeof(int));
   if (e != cudaSuccess) return cab::fail(CAB_ERR_LAUNCH, "device_status: %s", cudaGetErrorString(e));
-  *status = (value & cab::CAB_DEVICE_TIMEOUT) ? CAB_ERR_TIMEOUT : CAB_OK;
+  *status = (value & cab::CAB_DEVICE_TIMEOUT) ? CAB_ERR_TIMEOUT
+           : (value & cab::CAB_DEVICE_LAYOUT) ? CAB_ERR_LAUNCH
+                                               : CAB_OK;
   return CAB_OK;
 }

@@ -82,7 +82,7 @@ __device__ __forceinline__ double accumulate_chunk(const uint4& v, double acc) {
 }
 
 template <int kDtype>
-__global__ void __launch_bounds__(128) coarsen_kernel(const __grid_constant__ CUtensorMap qmap,
+__global__ void __launch_bounds__(256) coarsen_kernel(const __grid_constant__ CUtensorMap qmap,
                                                       const __grid_constant__ CUtensorMap kmap,
                                                       const Params p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -152,13 +152,24 @@ __global__ void __launch_bounds__(128) coarsen_kernel(const __grid_constant__ CU
     int best_row = 0x7fffffff;
     for (int r = lane; r < nvalid; r += 32) {
       const uint4* row = reinterpret_cast<const uint4*>(stage + static_cast<size_t>(r) * p.row_bytes);
-      double acc = 0.0;
+      // four independent partial sums: exact for bf16/f16 squares, so the result does
+      // not depend on how the chunks are split between them
+      double acc[4] = {0.0, 0.0, 0.0, 0.0};
       int c = lane % chunks;
-      for (int n = 0; n < chunks; ++n) {
-        acc = accumulate_chunk<kDtype>(row[c], acc);
+      int n = 0;
+      for (; n + 4 <= chunks; n += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          acc[u] = accumulate_chunk<kDtype>(row[c], acc[u]);
+          c = (c + 1 == chunks) ? 0 : c + 1;
+        }
+      }
+      for (; n < chunks; ++n) {
+        acc[0] = accumulate_chunk<kDtype>(row[c], acc[0]);
         c = (c + 1 == chunks) ? 0 : c + 1;
       }
-      if (acc > best) { best = acc; best_row = r; }
+      const double total = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+      if (total > best) { best = total; best_row = r; }
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
@@ -258,12 +269,14 @@ extern "C" int cab_coarsen_maxl2(const void* q, const void* k, void* q_coarse, v
   p.row_bytes = static_cast<int32_t>(row_bytes);
   p.stage_bytes = static_cast<int32_t>(row_bytes * block_size);
 
-  // Shared-memory budget: as many stages as fit in ~200 KB, at most 4 warps x 4 stages.
+  // Shared-memory budget: as many stages as fit in ~200 KB (at most 16), spread over up
+  // to 8 warps with two stages each so every warp keeps one block in flight while it
+  // reduces another.
   const int64_t budget = 200 * 1024;
   int64_t total_stages = std::min<int64_t>(16, budget / p.stage_bytes);
   if (total_stages < 1) return fail(CAB_ERR_UNSUPPORTED, "coarsen: block tile of %d bytes does not fit", p.stage_bytes);
-  p.warps = static_cast<int32_t>(std::min<int64_t>(4, total_stages));
-  p.stages = static_cast<int32_t>(std::min<int64_t>(4, total_stages / p.warps));
+  p.warps = static_cast<int32_t>(std::max<int64_t>(1, std::min<int64_t>(8, total_stages / 2)));
+  p.stages = static_cast<int32_t>(std::max<int64_t>(1, total_stages / p.warps));
   const size_t smem = static_cast<size_t>(p.warps) * p.stages * p.stage_bytes +
                       static_cast<size_t>(p.warps) * p.stages * sizeof(uint64_t);
 

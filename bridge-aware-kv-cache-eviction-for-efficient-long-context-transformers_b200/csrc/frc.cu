@@ -40,7 +40,8 @@ constexpr int kTileM = 128;
 constexpr int kTileN = 256;
 constexpr int kTileK = 64;
 constexpr int kStages = 4;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each drains half the columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kABytes = kTileM * kTileK * 2;  // 16 KB
 constexpr int kBBytes = kTileN * kTileK * 2;  // 32 KB
 constexpr int kStageBytes = kABytes + kBBytes;
@@ -224,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -311,7 +312,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int quad = warp & 3;              // TMEM lane quadrant this warp may access
+    const int colhalf = (warp - 2) >> 2;    // which 128 of the tile's 256 columns it drains
     int acc = 0;
     uint32_t acc_phase = 0;
     float vmax = -INFINITY, vmin_neg = -INFINITY;
@@ -342,8 +344,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after_sync();
       const int row = tm * kTileM + quad * 32 + lane;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * kTileN;
+      constexpr int kChunks = kTileN / 32 / 2;
 #pragma unroll 1
-      for (int c = 0; c < kTileN / 32; ++c) {
+      for (int c = colhalf * kChunks; c < (colhalf + 1) * kChunks; ++c) {
         uint32_t r[32];
         tmem_ld32(taddr + c * 32, r);
         tmem_wait_ld();

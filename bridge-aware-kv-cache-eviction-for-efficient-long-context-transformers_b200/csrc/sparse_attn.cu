@@ -122,8 +122,16 @@ struct Cfg {
   static constexpr int kKStages = D == 128 ? 3 : 4;
   static constexpr int kVStages = D == 128 ? 2 : 4;
   static constexpr int kTileBytes = kQBytes + kKStages * kKBytes + kVStages * kVBytes + kPBytes;
-  static constexpr int kSmem = kTileBytes + 1024 + 512;
+  static constexpr int kXchgBytes = 2 * 2 * 128 * 4;  // partial row maxima [parity][key block][row]
+  static constexpr int kAuxBytes = kXchgBytes + 256;   // + mbarriers, TMEM slot, abort flag
+  // Tiles start at the first 1024-byte boundary of the dynamic shared memory; the kernel
+  // checks at run time that tiles + aux fit in what it was given.
+  static constexpr int kSmemWanted = kTileBytes + kAuxBytes + 1024;
+  static constexpr int kSmem = kSmemWanted < 232448 ? kSmemWanted : 232448;
 };
+
+constexpr int kSoftmaxWarps = 8;
+constexpr int kAttnThreads = 64 + 32 * kSoftmaxWarps;
 
 struct Params {
   int32_t B, Hq, Hkv, N, M, P;
@@ -138,8 +146,12 @@ struct Params {
   int32_t causal;
 };
 
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 template <int D, bool kBF16>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kAttnThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, const Params p) {
   using C = Cfg<D>;
@@ -149,7 +161,16 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sK = sQ + C::kQBytes;
   uint8_t* sV = sK + C::kKStages * C::kKBytes;
   uint8_t* sP = sV + C::kVStages * C::kVBytes;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sP + C::kPBytes);
+  float* xchg = reinterpret_cast<float*>(sP + C::kPBytes);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sP + C::kPBytes + C::kXchgBytes);
+  {
+    uint32_t dyn;
+    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+    if (sP + C::kPBytes + C::kAuxBytes > smem_raw + dyn) {
+      if (threadIdx.x == 0) atomicOr(&g_device_status, CAB_DEVICE_LAYOUT);
+      return;  // shared memory base not aligned as expected: nothing was touched
+    }
+  }
   uint64_t* q_full = bar;
   uint64_t* q_empty = bar + 1;
   uint64_t* k_full = bar + 2;
@@ -174,10 +195,10 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(q_empty, 1);
     for (int s = 0; s < C::kKStages; ++s) { mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1); }
     for (int s = 0; s < C::kVStages; ++s) { mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1); }
-    for (int s = 0; s < 2; ++s) { mbar_init(&s_full[s], 1); mbar_init(&s_free[s], 4); }
-    mbar_init(p_full, 4);
+    for (int s = 0; s < 2; ++s) { mbar_init(&s_full[s], 1); mbar_init(&s_free[s], kSoftmaxWarps); }
+    mbar_init(p_full, kSoftmaxWarps);
     mbar_init(o_ready, 1);
-    mbar_init(o_free, 4);
+    mbar_init(o_free, kSoftmaxWarps);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -300,12 +321,19 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax + epilogue
+    // Warp w (2..9) owns TMEM lane quadrant w & 3 (rows 32*(w&3) .. +31 of the 128-row
+    // tile) and key block kb = (w - 2) / 4 of every 128-key tile (columns 64*kb .. +63).
+    // The two threads holding the two halves of a row swap partial row maxima through
+    // shared memory (double-buffered by tile parity) under a 64-thread named barrier.
     const int quad = warp & 3;
+    const int kb = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
     const int half = r >> 6;
+    const int pair_bar = 1 + quad;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-    uint8_t* prow = sP + r * 128;
-    uint32_t gi = 0, gt = 0;
+    uint8_t* prow = sP + kb * 16384 + r * 128;
+    constexpr int kHalfD = D / 2;
+    uint32_t gt = 0;
     for (int64_t item = blockIdx.x; item < p.items; item += gridDim.x) {
       const int T = p.ntiles[item];
       const int bh = static_cast<int>(item / p.P), pr = static_cast<int>(item % p.P);
@@ -313,50 +341,56 @@ __global__ void __launch_bounds__(192, 1)
       const int row = 128 * pr + r;
       const int64_t ooff = b * p.o_s0 + h * p.o_s1 + static_cast<int64_t>(row) * p.o_s2;
       using OutT = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
-      OutT* orow = reinterpret_cast<OutT*>(p.out) + ooff;
+      OutT* orow = reinterpret_cast<OutT*>(p.out) + ooff + kb * kHalfD;
       if (T == 0) {
         if (row < p.N) {
 #pragma unroll
-          for (int c = 0; c < D; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
-          if (p.lse) p.lse[static_cast<int64_t>(bh) * p.N + row] = -INFINITY;
+          for (int c = 0; c < kHalfD; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
+          if (p.lse && kb == 0) p.lse[static_cast<int64_t>(bh) * p.N + row] = -INFINITY;
         }
         continue;
       }
       const uint32_t* ul = p.ulist + item * p.stride;
       float m_run = -INFINITY, l = 0.f;
       bool ok = true;
+      uint32_t e_next = ul[kb];
       for (int t = 0; t < T; ++t) {
         const uint32_t g = gt + t, buf = g & 1;
-        const uint32_t e0 = ul[2 * t], e1 = ul[2 * t + 1];
-        int lim[2];
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          const uint32_t e = x ? e1 : e0;
-          const int j = static_cast<int>(e & kIdxMask);
-          int n = ((e >> (30 + half)) & 1u) ? min(64, p.N - 64 * j) : 0;
-          if (p.causal) n = min(n, row - 64 * j + 1);
-          lim[x] = max(n, 0);
-        }
+        const uint32_t e = e_next;
+        if (t + 1 < T) e_next = ul[2 * (t + 1) + kb];
+        const int j = static_cast<int>(e & kIdxMask);
+        int lim = ((e >> (30 + half)) & 1u) ? min(64, p.N - 64 * j) : 0;
+        if (p.causal) lim = min(lim, row - 64 * j + 1);
+        lim = max(lim, 0);
+        const bool any_live = __any_sync(0xffffffffu, lim > 0);
+        const bool all_full = __all_sync(0xffffffffu, lim >= 64);
+
         const bool okw = mbar_wait(&s_full[buf], (g >> 1) & 1, abort_flag);
         if (!__all_sync(0xffffffffu, okw)) { ok = false; break; }
         tc_fence_after_sync();
-        uint32_t s[128];
-        tmem_ld32(tmem + lane_addr + buf * 128 + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-        tmem_ld32(tmem + lane_addr + buf * 128 + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
-        tmem_ld32(tmem + lane_addr + buf * 128 + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
-        tmem_ld32(tmem + lane_addr + buf * 128 + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
-        tmem_wait_ld();
+        uint32_t s[64];
+        if (any_live) {
+          tmem_ld32(tmem + lane_addr + buf * 128 + kb * 64, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+          tmem_ld32(tmem + lane_addr + buf * 128 + kb * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+          tmem_wait_ld();
+        }
         tc_fence_before_sync();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[buf]);
 
         float mx = -INFINITY;
+        if (all_full) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          const bool valid = (c < 64) ? (c < lim[0]) : (c - 64 < lim[1]);
-          if (valid) mx = fmaxf(mx, __uint_as_float(s[c]));
+          for (int c = 0; c < 64; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
+        } else if (any_live) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (c < lim) mx = fmaxf(mx, __uint_as_float(s[c]));
         }
-        const float m_tile = mx * p.scale_log2;  // -inf stays -inf (scale > 0)
+        float* xs = xchg + (t & 1) * 256;
+        xs[kb * 128 + r] = mx;
+        named_bar_sync(pair_bar, 64);
+        const float m_tile = fmaxf(mx, xs[(kb ^ 1) * 128 + r]) * p.scale_log2;  // -inf stays -inf
         float alpha = 1.f;
         bool need = false;
         if (m_run == -INFINITY) {
@@ -367,23 +401,41 @@ __global__ void __launch_bounds__(192, 1)
           m_run = m_tile;
           l *= alpha;
         }
-        const bool live = m_run != -INFINITY;
-        uint32_t pk[64];
+        uint32_t pk[32];
         float lsum = 0.f;
+        if (all_full) {
+          const float nm = -m_run;
 #pragma unroll
-        for (int c = 0; c < 128; c += 2) {
-          const bool v0 = (c < 64) ? (c < lim[0]) : (c - 64 < lim[1]);
-          const bool v1 = (c + 1 < 64) ? (c + 1 < lim[0]) : (c + 1 - 64 < lim[1]);
-          const float p0 = (v0 && live) ? ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, -m_run)) : 0.f;
-          const float p1 = (v1 && live) ? ex2(fmaf(__uint_as_float(s[c + 1]), p.scale_log2, -m_run)) : 0.f;
-          lsum += p0 + p1;
-          if constexpr (kBF16) {
-            __nv_bfloat162 v2 = __floats2bfloat162_rn(p0, p1);
-            pk[c >> 1] = *reinterpret_cast<uint32_t*>(&v2);
-          } else {
-            __half2 v2 = __floats2half2_rn(p0, p1);
-            pk[c >> 1] = *reinterpret_cast<uint32_t*>(&v2);
+          for (int c = 0; c < 64; c += 2) {
+            const float p0 = ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, nm));
+            const float p1 = ex2(fmaf(__uint_as_float(s[c + 1]), p.scale_log2, nm));
+            lsum += p0 + p1;
+            if constexpr (kBF16) {
+              __nv_bfloat162 v2 = __floats2bfloat162_rn(p0, p1);
+              pk[c >> 1] = *reinterpret_cast<uint32_t*>(&v2);
+            } else {
+              __half2 v2 = __floats2half2_rn(p0, p1);
+              pk[c >> 1] = *reinterpret_cast<uint32_t*>(&v2);
+            }
           }
+        } else if (any_live) {
+          const bool live = m_run != -INFINITY;
+#pragma unroll
+          for (int c = 0; c < 64; c += 2) {
+            const float p0 = (c < lim && live) ? ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, -m_run)) : 0.f;
+            const float p1 = (c + 1 < lim && live) ? ex2(fmaf(__uint_as_float(s[c + 1]), p.scale_log2, -m_run)) : 0.f;
+            lsum += p0 + p1;
+            if constexpr (kBF16) {
+              __nv_bfloat162 v2 = __floats2bfloat162_rn(p0, p1);
+              pk[c >> 1] = *reinterpret_cast<uint32_t*>(&v2);
+            } else {
+              __half2 v2 = __floats2half2_rn(p0, p1);
+              pk[c >> 1] = *reinterpret_cast<uint32_t*>(&v2);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) pk[c] = 0u;
         }
         l += lsum;
 
@@ -394,43 +446,46 @@ __global__ void __launch_bounds__(192, 1)
         }
         if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
-          for (int c = 0; c < D; c += 32) {
-            uint32_t o[32];
-            tmem_ld32(tmem_o + lane_addr + c, o);
+          for (int c = kb * kHalfD; c < (kb + 1) * kHalfD; c += 16) {
+            uint32_t o[16];
+            tmem_ld16(tmem_o + lane_addr + c, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int x = 0; x < 32; ++x) o[x] = __float_as_uint(__uint_as_float(o[x]) * alpha);
-            tmem_st32(tmem_o + lane_addr + c, o);
+            for (int x = 0; x < 16; ++x) o[x] = __float_as_uint(__uint_as_float(o[x]) * alpha);
+            tmem_st16(tmem_o + lane_addr + c, o);
           }
           tmem_wait_st();
         }
-        // P row -> 128-byte-swizzled K-major tile (two 64-key atoms of 16 KB)
+        // this thread's 64 keys of P -> one 128-byte-swizzled K-major atom row
 #pragma unroll
-        for (int ch = 0; ch < 16; ++ch) {
-          const int atom = ch >> 3, cc = ch & 7;
-          uint4 v = make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-          *reinterpret_cast<uint4*>(prow + atom * 16384 + ((cc ^ (r & 7)) << 4)) = v;
-        }
+        for (int cc = 0; cc < 8; ++cc)
+          *reinterpret_cast<uint4*>(prow + ((cc ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
         fence_proxy_async_smem();
         tc_fence_before_sync();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full);
       }
       if (!ok) break;
-      // ---- epilogue: O / l
+      // ---- epilogue: O / l, each thread writes its half of the row's D columns
       const uint32_t glast = gt + T - 1;
       const bool oko = mbar_wait(o_ready, glast & 1, abort_flag);
       if (!__all_sync(0xffffffffu, oko)) break;
       tc_fence_after_sync();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      float* xs = xchg + (T & 1) * 256;
+      xs[kb * 128 + r] = l;
+      named_bar_sync(pair_bar, 64);
+      const float l_row = l + xs[(kb ^ 1) * 128 + r];
+      named_bar_sync(pair_bar, 64);  // both have read before either reuses the buffer
+      const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
 #pragma unroll
-      for (int c = 0; c < D; c += 32) {
-        uint32_t o[32];
-        tmem_ld32(tmem_o + lane_addr + c, o);
+      for (int c = 0; c < kHalfD; c += 16) {
+        uint32_t o[16];
+        tmem_ld16(tmem_o + lane_addr + kb * kHalfD + c, o);
         tmem_wait_ld();
         if (row < p.N) {
 #pragma unroll
-          for (int x = 0; x < 32; x += 8) {
+          for (int x = 0; x < 16; x += 8) {
             uint32_t w[4];
 #pragma unroll
             for (int y = 0; y < 4; ++y) {
@@ -447,13 +502,12 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
-      if (row < p.N && p.lse)
-        p.lse[static_cast<int64_t>(bh) * p.N + row] = l > 0.f ? (m_run + __log2f(l)) * kLn2 : -INFINITY;
+      if (row < p.N && p.lse && kb == 0)
+        p.lse[static_cast<int64_t>(bh) * p.N + row] = l_row > 0.f ? (m_run + __log2f(l_row)) * kLn2 : -INFINITY;
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(o_free);
       gt += T;
-      ++gi;
     }
   }
   tc_fence_before_sync();
@@ -584,7 +638,7 @@ static int launch_tc(const CUtensorMap& qm, const CUtensorMap& km, const CUtenso
   auto kern = attn_tc_kernel<D, kBF16>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::kSmem);
   const int grid = static_cast<int>(std::min<int64_t>(p.items, current_sm_count()));
-  kern<<<grid, 192, Cfg<D>::kSmem, st>>>(qm, km, vm, p);
+  kern<<<grid, kAttnThreads, Cfg<D>::kSmem, st>>>(qm, km, vm, p);
   return check_launch("attn_tc_kernel");
 }
 

@@ -4,11 +4,12 @@
 // row once (coalesced, 16-byte loads when M % 4 == 0) and stores it in shared memory as
 // order-preserving 32-bit keys: the preferred direction (select_high or not) maps to
 // "larger key", NaN to the least preferred real key, -0 to +0, excluded (causal j > i)
-// candidates to 0 and the forced diagonal to 0xFFFFFFFF. A four-pass MSB-first radix
-// select (256-bin shared-memory histogram, warp-aggregated atomics) finds the k_i-th
-// largest key tau. A final pass in index order takes every key > tau and the lowest-index
-// keys == tau until k_i are taken, compacting with ballots so kv_idx comes out ascending,
-// and writes the dense 0/1 mask of the row.
+// candidates to 0 and the forced diagonal to 0xFFFFFFFF. An MSB-first radix select over
+// the ordinary keys (8-bit digits, 256-bin shared-memory histogram) starts at the highest
+// bit in which the row's keys differ and stops as soon as the boundary bin is taken
+// whole, which gives the threshold tau. A final pass in index order takes every key >
+// tau and the lowest-index keys == tau until k_i are taken, compacting with ballots so
+// kv_idx comes out ascending, and writes the dense 0/1 mask of the row.
 //
 // Selection rule: per-(b,h,row) top-k of the Forman-Ricci score (generate_block_mask,
 // called with select_high / keep_diagonal / causal at experiments/longbench_qa/
@@ -87,60 +88,104 @@ __global__ void __launch_bounds__(256) topk_kernel(const Params p) {
     }
     __syncwarp();
 
-    // ---- radix select of the kk-th largest key
-    uint32_t prefix = 0u, pmask = 0u;
-    int remaining = kk;
-#pragma unroll 1
-    for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int b = lane; b < 256; b += 32) hist[b] = 0u;
-      __syncwarp();
-      for (int base = 0; base < M; base += 32) {
-        const int j = base + lane;
-        const uint32_t key = j < M ? keys[j] : 0u;
-        const bool match = j < M && (key & pmask) == prefix;
-        const uint32_t digit = match ? ((key >> shift) & 255u) : 0x100u;
-        const uint32_t peers = __match_any_sync(0xffffffffu, digit);
-        if (match && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
+    // ---- radix select among the ordinary keys (the forced diagonal is always taken,
+    // excluded candidates never are). Passes start at the highest bit in which the
+    // row's ordinary keys differ, so bits every key shares cost nothing.
+    uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
+    for (int j = lane; j < M; j += 32) {
+      const uint32_t key = keys[j];
+      if (key != 0u && key != 0xFFFFFFFFu) {
+        kmin = min(kmin, key);
+        kmax = max(kmax, key);
       }
-      __syncwarp();
-      // lane l owns bins 255-8l .. 248-8l (highest bins first)
-      uint32_t c[8];
-      uint32_t tot = 0;
-#pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        c[t] = hist[255 - 8 * lane - t];
-        tot += c[t];
-      }
-      uint32_t incl = tot;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const uint32_t o = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += o;
-      }
-      uint32_t running = incl - tot;
-      int found_digit = -1;
-      uint32_t found_above = 0;
-#pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        if (found_digit < 0 && running < static_cast<uint32_t>(remaining) &&
-            running + c[t] >= static_cast<uint32_t>(remaining)) {
-          found_digit = 255 - 8 * lane - t;
-          found_above = running;
-        }
-        running += c[t];
-      }
-      const uint32_t who = __ballot_sync(0xffffffffu, found_digit >= 0);
-      const int src_lane = __ffs(who) - 1;
-      const int digit = __shfl_sync(0xffffffffu, found_digit, src_lane);
-      const uint32_t above = __shfl_sync(0xffffffffu, found_above, src_lane);
-      prefix |= static_cast<uint32_t>(digit) << shift;
-      pmask |= 255u << shift;
-      remaining -= static_cast<int>(above);
-      __syncwarp();
     }
-    const uint32_t tau = prefix;
-    const int take_eq = remaining;  // keys == tau to take, lowest index first
-
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, off));
+      kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, off));
+    }
+    const int forced = (p.keep_diagonal && i < ncand) ? 1 : 0;
+    int remaining = kk - forced;
+    // Selection rule applied below: take key > tau, and among keys == tau the lowest
+    // `take_eq` indices.
+    uint32_t tau = 0xFFFFFFFEu;  // only the forced key (0xFFFFFFFF) is above this
+    int take_eq = 0;
+    if (remaining > 0) {
+      const uint32_t diff = kmin ^ kmax;
+      if (diff == 0u) {
+        tau = kmin;
+        take_eq = remaining;
+      } else {
+        int hi = 31 - __clz(diff);  // highest differing bit; bits above it are shared
+        uint32_t prefix = hi == 31 ? 0u : (kmin & ~((2u << hi) - 1u));
+        uint32_t pmask = hi == 31 ? 0u : ~((2u << hi) - 1u);
+        bool resolved = false;
+#pragma unroll 1
+        while (!resolved) {
+          const int width = min(8, hi + 1);
+          const int lo = hi + 1 - width;
+          const uint32_t dmask = (1u << width) - 1u;
+          for (int b = lane; b < 256; b += 32) hist[b] = 0u;
+          __syncwarp();
+          for (int j = lane; j < M; j += 32) {
+            const uint32_t key = keys[j];
+            if (key != 0u && key != 0xFFFFFFFFu && (key & pmask) == prefix)
+              atomicAdd(&hist[(key >> lo) & dmask], 1u);
+          }
+          __syncwarp();
+          // lane l owns bins 255-8l .. 248-8l (highest first)
+          uint32_t c[8];
+          uint32_t tot = 0;
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            c[t] = hist[255 - 8 * lane - t];
+            tot += c[t];
+          }
+          uint32_t incl = tot;
+#pragma unroll
+          for (int off = 1; off < 32; off <<= 1) {
+            const uint32_t o = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= off) incl += o;
+          }
+          uint32_t running = incl - tot;
+          int found_digit = -1;
+          uint32_t found_above = 0, found_count = 0;
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            if (found_digit < 0 && running < static_cast<uint32_t>(remaining) &&
+                running + c[t] >= static_cast<uint32_t>(remaining)) {
+              found_digit = 255 - 8 * lane - t;
+              found_above = running;
+              found_count = c[t];
+            }
+            running += c[t];
+          }
+          const uint32_t who = __ballot_sync(0xffffffffu, found_digit >= 0);
+          const int src_lane = __ffs(who) - 1;
+          const uint32_t digit = static_cast<uint32_t>(__shfl_sync(0xffffffffu, found_digit, src_lane));
+          const uint32_t above = __shfl_sync(0xffffffffu, found_above, src_lane);
+          const uint32_t count = __shfl_sync(0xffffffffu, found_count, src_lane);
+          prefix |= digit << lo;
+          pmask |= dmask << lo;
+          remaining -= static_cast<int>(above);
+          __syncwarp();
+          if (static_cast<uint32_t>(remaining) == count) {
+            // the whole boundary bin is taken: every ordinary key >= prefix (low bits
+            // zero). Ordinary keys are >= 0x007FFFFF, so tau = 0 still leaves the
+            // excluded candidates (key 0) out.
+            tau = prefix == 0u ? 0u : prefix - 1u;
+            take_eq = 0;
+            resolved = true;
+          } else if (lo == 0) {
+            tau = prefix;  // exact boundary key; ties by index
+            take_eq = remaining;
+            resolved = true;
+          } else {
+            hi = lo - 1;
+          }
+        }
+      }
+    }
     // ---- select in index order, compact, write outputs
     int32_t* out_idx = p.kv_idx + row * p.k;
     uint8_t* out_dense = p.dense ? p.dense + row * M : nullptr;

@@ -76,7 +76,8 @@ CAB_API const char* cab_last_error_string(void);
 CAB_API int cab_device_supported(int device);
 
 /* Synchronises `stream`, then stores and clears the device-side status word of the
- * current device (0 = fine, CAB_ERR_TIMEOUT if a kernel's bounded wait gave up). */
+ * current device (0 = fine, CAB_ERR_TIMEOUT if a kernel's bounded wait gave up,
+ * CAB_ERR_LAUNCH if a kernel found its shared-memory layout did not fit and did nothing). */
 CAB_API int cab_device_status(void* stream, int* status);
 
 /*
