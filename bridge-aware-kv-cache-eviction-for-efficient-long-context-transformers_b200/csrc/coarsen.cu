@@ -4,11 +4,12 @@
 // memory stages; lane 0 fills them with TMA tiled loads (box = block_size rows x D
 // columns of one head), so every byte of Q and K is read from HBM exactly once and the
 // warp's next blocks are in flight while it reduces the current one. In a stage, lane l
-// owns rows l, l+32, ...: it accumulates the row's squared L2 norm in fp64 (exact for
-// bf16/f16 inputs, so the choice does not depend on summation order), reading its
-// 16-byte chunks in a lane-rotated order so the 8 lanes of a shared-memory phase hit
-// distinct banks. A warp arg-max (lowest index on ties) picks the token, whose row is
-// then copied from shared memory to the dense output.
+// owns rows l, l+32, ...: it accumulates each row's squared L2 norm in fp32 (FFMA),
+// reading its 16-byte chunks in a lane-rotated order so the 8 lanes of a shared-memory
+// phase hit distinct banks, and a warp arg-max picks the best row. Every row whose fp32
+// norm lies within the fp32 error bound of that maximum is then re-scored in fp64, which
+// is exact for bf16/f16 inputs, so the chosen token (lowest index on exact ties) is the
+// one exact arithmetic picks. Its row is copied from shared memory to the dense output.
 //
 // Semantics follow the reference's Max-L2 pooling (README.md:30-32;
 // CAB_Attention_Colab.ipynb cells 5-7: one representative token per block chosen by L2
@@ -81,6 +82,54 @@ __device__ __forceinline__ double accumulate_chunk(const uint4& v, double acc) {
   return acc;
 }
 
+// fp32 variant: bf16 / f16 squares are exact in fp32 and only the additions round.
+template <int kDtype>
+__device__ __forceinline__ float accumulate_chunk32(const uint4& v, float acc) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (kDtype == CAB_DTYPE_BF16) {
+      const float lo = __uint_as_float(w[i] << 16), hi = __uint_as_float(w[i] & 0xFFFF0000u);
+      acc = fmaf(lo, lo, acc);
+      acc = fmaf(hi, hi, acc);
+    } else if constexpr (kDtype == CAB_DTYPE_F16) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      acc = fmaf(f.x, f.x, acc);
+      acc = fmaf(f.y, f.y, acc);
+    } else {
+      const float a = __uint_as_float(w[i]);
+      acc = fmaf(a, a, acc);
+    }
+  }
+  return acc;
+}
+
+// Exact (fp64) squared norm of one row; chunk order rotated by `start`.
+template <int kDtype>
+__device__ __forceinline__ double row_norm64(const uint4* row, int chunks, int start) {
+  double acc[4] = {0.0, 0.0, 0.0, 0.0};
+  int c = start, n = 0;
+  for (; n + 4 <= chunks; n += 4) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      acc[u] = accumulate_chunk<kDtype>(row[c], acc[u]);
+      c = (c + 1 == chunks) ? 0 : c + 1;
+    }
+  }
+  for (; n < chunks; ++n) {
+    acc[0] = accumulate_chunk<kDtype>(row[c], acc[0]);
+    c = (c + 1 == chunks) ? 0 : c + 1;
+  }
+  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+}
+
+// Candidate margin of the fp32 pass: each fp32 norm is a sum of at most 512 / 4 + 3
+// rounded terms (D * elem <= 1024 bytes, four partial sums), so its relative error is
+// below gamma = 131 * 2^-24 < 8e-6 while no square under- or overflows; a row can only
+// match or beat the fp32 arg-max exactly if its fp32 norm is >= (1 - 2 gamma) of it.
+constexpr float kCandidateMargin = 4e-5f;
+constexpr int kMaxRowsPerLane = 8;  // block_size <= 256
+
 template <int kDtype>
 __global__ void __launch_bounds__(256) coarsen_kernel(const __grid_constant__ CUtensorMap qmap,
                                                       const __grid_constant__ CUtensorMap kmap,
@@ -148,34 +197,69 @@ __global__ void __launch_bounds__(256) coarsen_kernel(const __grid_constant__ CU
     const int m = static_cast<int>(idx % p.M);
     const int nvalid = min(p.bs, p.N - m * p.bs);
 
-    double best = -1.0;
+    // Pass 1: fp32 norms (FFMA), arg-max with the lowest index on ties.
+    const int start = lane % chunks;
+    float n32[kMaxRowsPerLane];
+    float best32 = -1.0f;
     int best_row = 0x7fffffff;
-    for (int r = lane; r < nvalid; r += 32) {
-      const uint4* row = reinterpret_cast<const uint4*>(stage + static_cast<size_t>(r) * p.row_bytes);
-      // four independent partial sums: exact for bf16/f16 squares, so the result does
-      // not depend on how the chunks are split between them
-      double acc[4] = {0.0, 0.0, 0.0, 0.0};
-      int c = lane % chunks;
-      int n = 0;
-      for (; n + 4 <= chunks; n += 4) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          acc[u] = accumulate_chunk<kDtype>(row[c], acc[u]);
+    for (int x = 0; x < kMaxRowsPerLane; ++x) {
+      const int r = lane + 32 * x;
+      n32[x] = -1.0f;
+      if (r < nvalid) {
+        const uint4* row = reinterpret_cast<const uint4*>(stage + static_cast<size_t>(r) * p.row_bytes);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        int c = start, n = 0;
+        for (; n + 4 <= chunks; n += 4) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            acc[u] = accumulate_chunk32<kDtype>(row[c], acc[u]);
+            c = (c + 1 == chunks) ? 0 : c + 1;
+          }
+        }
+        for (; n < chunks; ++n) {
+          acc[0] = accumulate_chunk32<kDtype>(row[c], acc[0]);
           c = (c + 1 == chunks) ? 0 : c + 1;
         }
+        const float tot = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+        n32[x] = tot;
+        if (tot > best32) { best32 = tot; best_row = r; }
       }
-      for (; n < chunks; ++n) {
-        acc[0] = accumulate_chunk<kDtype>(row[c], acc[0]);
-        c = (c + 1 == chunks) ? 0 : c + 1;
-      }
-      const double total = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-      if (total > best) { best = total; best_row = r; }
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
-      const double ob = __shfl_xor_sync(0xffffffffu, best, off);
+      const float ob = __shfl_xor_sync(0xffffffffu, best32, off);
       const int orow = __shfl_xor_sync(0xffffffffu, best_row, off);
-      if (ob > best || (ob == best && orow < best_row)) { best = ob; best_row = orow; }
+      if (ob > best32 || (ob == best32 && orow < best_row)) { best32 = ob; best_row = orow; }
+    }
+    // Pass 2: rows within the fp32 error margin of the arg-max (all rows when the norms
+    // are not safely inside fp32 range) are re-scored exactly in fp64.
+    const bool safe = best32 >= 1e-30f && best32 <= 3.0e38f;
+    const float thr = safe ? best32 * (1.0f - kCandidateMargin) : -2.0f;
+    uint32_t cand = 0u;
+#pragma unroll
+    for (int x = 0; x < kMaxRowsPerLane; ++x)
+      if (lane + 32 * x < nvalid && !(n32[x] < thr)) cand |= 1u << x;
+    const int ncand = __reduce_add_sync(0xffffffffu, static_cast<unsigned>(__popc(cand)));
+    if (ncand > 1) {
+      double best = -1.0;
+      best_row = 0x7fffffff;
+#pragma unroll 1
+      for (int x = 0; x < kMaxRowsPerLane; ++x) {
+        if (!((cand >> x) & 1u)) continue;
+        const int r = lane + 32 * x;
+        // same chunk order in every lane, so identical rows get identical sums even for
+        // fp32 inputs (whose fp64 sums of squares are not exact)
+        const double tot = row_norm64<kDtype>(
+            reinterpret_cast<const uint4*>(stage + static_cast<size_t>(r) * p.row_bytes), chunks, 0);
+        if (tot > best) { best = tot; best_row = r; }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const double ob = __shfl_xor_sync(0xffffffffu, best, off);
+        const int orow = __shfl_xor_sync(0xffffffffu, best_row, off);
+        if (ob > best || (ob == best && orow < best_row)) { best = ob; best_row = orow; }
+      }
     }
     if (best_row >= nvalid) best_row = 0;  // every valid row was NaN: keep the first
 

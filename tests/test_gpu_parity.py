@@ -55,6 +55,14 @@ def test_coarsen_bit_exact(dt, B, Hq, Hkv, N, D, bs):
     # exact ties inside a block: duplicate a token, and a permuted copy (equal norm)
     q[0, 0, 1] = q[0, 0, 0]
     k[0, 0, 3] = k[0, 0, 2].flip(-1)
+    # near tie: one element one ulp larger, so fp32 norms may tie but exact ones differ
+    near = k[0, 0, 2].clone()
+    near[0] = torch.nextafter(near[0].float(), torch.tensor(float("inf"))).to(near.dtype) \
+        if DT[dt] == torch.float32 else (near[0].float() * (1 + 2 ** -7)).to(near.dtype)
+    k[0, 0, 5] = near
+    # a whole block of identical tokens: every fp32 norm ties, the lowest index wins
+    if N >= 2 * bs:
+        q[0, 0, bs:2 * bs] = q[0, 0, bs]
     qc, kc, qi, ki = coarsen_qk_max_l2(q.cuda(), k.cuda(), bs, return_indices=True)
     oq, oqi = orc.coarsen_maxl2(np_of(q), bs)
     ok, oki = orc.coarsen_maxl2(np_of(k), bs)
