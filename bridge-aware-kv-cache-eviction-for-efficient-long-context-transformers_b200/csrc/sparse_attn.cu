@@ -118,8 +118,8 @@ struct Cfg {
   static constexpr int kQBytes = 128 * D * 2;
   static constexpr int kKBytes = 128 * D * 2;
   static constexpr int kVBytes = 128 * D * 2;
-  static constexpr int kPBytes = 128 * 128 * 2;
-  static constexpr int kKStages = D == 128 ? 3 : 4;
+  static constexpr int kPBytes = 2 * 128 * 128 * 2;  // two P buffers (tile parity)
+  static constexpr int kKStages = D == 128 ? 2 : 4;
   static constexpr int kVStages = D == 128 ? 2 : 4;
   static constexpr int kTileBytes = kQBytes + kKStages * kKBytes + kVStages * kVBytes + kPBytes;
   static constexpr int kXchgBytes = 2 * 2 * 128 * 4;  // partial row maxima [parity][key block][row]
@@ -130,6 +130,7 @@ struct Cfg {
   static constexpr int kSmem = kSmemWanted < 232448 ? kSmemWanted : 232448;
 };
 
+// Warp 0: TMA producer; warp 1: MMA issuer; warps 2-9: softmax.
 constexpr int kSoftmaxWarps = 8;
 constexpr int kAttnThreads = 64 + 32 * kSoftmaxWarps;
 
@@ -145,6 +146,17 @@ struct Params {
   float scale_log2;
   int32_t causal;
 };
+
+template <bool kBF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if constexpr (kBF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
@@ -296,10 +308,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             if (t == 1 && gi > 0 && !mbar_wait(o_free, (gi - 1) & 1, abort_flag)) { ok = false; break; }
             tc_fence_after_sync();
             const uint32_t vb = aV + vs * C::kVBytes;
+            const uint32_t pb = aP + (g & 1) * (C::kPBytes / 2);  // P buffer of this tile
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
               const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-              mma_f16_ss(tmem_o, make_smem_desc(aP + aoff, 16, 1024, 2),
+              mma_f16_ss(tmem_o, make_smem_desc(pb + aoff, 16, 1024, 2),
                          make_smem_desc(vb + kk * 2048, 16384, 1024, 2), idesc_o,
                          (t > 1 || kk > 0) ? 1u : 0u);
             }
@@ -378,15 +391,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[buf]);
 
-        float mx = -INFINITY;
+        // row max over this thread's 64 keys: eight independent chains, then a tree
+        float mx8[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mx8[u] = -INFINITY;
         if (all_full) {
 #pragma unroll
-          for (int c = 0; c < 64; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
+          for (int c = 0; c < 64; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(s[c]));
         } else if (any_live) {
 #pragma unroll
           for (int c = 0; c < 64; ++c)
-            if (c < lim) mx = fmaxf(mx, __uint_as_float(s[c]));
+            if (c < lim) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(s[c]));
         }
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         float* xs = xchg + (t & 1) * 256;
         xs[kb * 128 + r] = mx;
         named_bar_sync(pair_bar, 64);
@@ -401,44 +419,50 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           m_run = m_tile;
           l *= alpha;
         }
-        uint32_t pk[32];
-        float lsum = 0.f;
+        // P of this tile goes to buffer g & 1. That buffer was last read by PV(g - 2),
+        // which completed before S(g) did (one issuing thread, in-order tensor pipe), so
+        // it is free now. Eight keys at a time: exp2 -> pack -> one 16-byte store.
+        uint8_t* pdst = prow + (g & 1) * (C::kPBytes / 2);
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
         if (all_full) {
           const float nm = -m_run;
 #pragma unroll
-          for (int c = 0; c < 64; c += 2) {
-            const float p0 = ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, nm));
-            const float p1 = ex2(fmaf(__uint_as_float(s[c + 1]), p.scale_log2, nm));
-            lsum += p0 + p1;
-            if constexpr (kBF16) {
-              __nv_bfloat162 v2 = __floats2bfloat162_rn(p0, p1);
-              pk[c >> 1] = *reinterpret_cast<uint32_t*>(&v2);
-            } else {
-              __half2 v2 = __floats2half2_rn(p0, p1);
-              pk[c >> 1] = *reinterpret_cast<uint32_t*>(&v2);
+          for (int cc = 0; cc < 8; ++cc) {
+            uint32_t w[4];
+#pragma unroll
+            for (int y = 0; y < 4; ++y) {
+              const int c = 8 * cc + 2 * y;
+              const float p0 = ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, nm));
+              const float p1 = ex2(fmaf(__uint_as_float(s[c + 1]), p.scale_log2, nm));
+              ls[y] += p0 + p1;
+              w[y] = pack2<kBF16>(p0, p1);
             }
+            *reinterpret_cast<uint4*>(pdst + ((cc ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
           }
         } else if (any_live) {
           const bool live = m_run != -INFINITY;
 #pragma unroll
-          for (int c = 0; c < 64; c += 2) {
-            const float p0 = (c < lim && live) ? ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, -m_run)) : 0.f;
-            const float p1 = (c + 1 < lim && live) ? ex2(fmaf(__uint_as_float(s[c + 1]), p.scale_log2, -m_run)) : 0.f;
-            lsum += p0 + p1;
-            if constexpr (kBF16) {
-              __nv_bfloat162 v2 = __floats2bfloat162_rn(p0, p1);
-              pk[c >> 1] = *reinterpret_cast<uint32_t*>(&v2);
-            } else {
-              __half2 v2 = __floats2half2_rn(p0, p1);
-              pk[c >> 1] = *reinterpret_cast<uint32_t*>(&v2);
+          for (int cc = 0; cc < 8; ++cc) {
+            uint32_t w[4];
+#pragma unroll
+            for (int y = 0; y < 4; ++y) {
+              const int c = 8 * cc + 2 * y;
+              const float p0 = (c < lim && live) ? ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, -m_run)) : 0.f;
+              const float p1 = (c + 1 < lim && live) ? ex2(fmaf(__uint_as_float(s[c + 1]), p.scale_log2, -m_run)) : 0.f;
+              ls[y] += p0 + p1;
+              w[y] = pack2<kBF16>(p0, p1);
             }
+            *reinterpret_cast<uint4*>(pdst + ((cc ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
           }
         } else {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) pk[c] = 0u;
+          for (int cc = 0; cc < 8; ++cc)
+            *reinterpret_cast<uint4*>(pdst + ((cc ^ (r & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
         }
-        l += lsum;
+        l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
 
+        // O may only be rescaled once PV(g - 1) has finished accumulating into it. The
+        // wait sits at the end of the tile: PV(g - 1) ran while this tile's exps did.
         if (t > 0) {
           const bool okp = mbar_wait(o_ready, (g - 1) & 1, abort_flag);
           if (!__all_sync(0xffffffffu, okp)) { ok = false; break; }
@@ -456,11 +480,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
           tmem_wait_st();
         }
-        // this thread's 64 keys of P -> one 128-byte-swizzled K-major atom row
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc)
-          *reinterpret_cast<uint4*>(prow + ((cc ^ (r & 7)) << 4)) =
-              make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
         fence_proxy_async_smem();
         tc_fence_before_sync();
         __syncwarp();
