@@ -7,14 +7,16 @@
 //    block 2p / by block 2p+1); key blocks are consumed two at a time (a 128-key tile).
 //    A block kept by only one of the two query blocks is masked for the other 64 rows.
 //  * Warp 0 streams Q (once per item), K and V tiles with TMA (128-byte swizzle) into
-//    3/2-stage (D=128) or 4/4-stage (D=64) shared-memory rings. One thread of warp 1
-//    issues S = Q K^T (M=128, N=128, K=D) into one of two TMEM S buffers and, one tile
-//    behind, O += P V (M=128, N=D, K=128, V read MN-major straight from its natural
-//    [keys, D] layout) into a TMEM O accumulator, so S(t+1) overlaps the softmax of t.
-//  * Warps 2-5 own one query row per thread: tcgen05.ld of the S row, exact masking
-//    (flags, causal token mask, sequence end), online softmax in the exp2 domain with a
-//    lazy rescale of O (only when the running max grows by more than 2^8), P written as
-//    bf16/f16 into a 128-byte-swizzled shared tile, and the final O / l epilogue.
+//    3-stage (D=128) or 4-stage (D=64) shared-memory rings. One thread of warp 1 issues
+//    S = Q K^T (M=128, N=128, K=D, both operands in shared memory) into one of two TMEM
+//    S buffers and, one tile behind, O += P V with P read from TMEM and V read MN-major
+//    from its natural [keys, D] layout (M=128, N=D, K=128), so S(t+1) overlaps the
+//    softmax of t and P never touches shared memory (whose bandwidth the tensor core,
+//    TMA and softmax would otherwise share).
+//  * Warps 2-9, two per row (one per 64-key block of the tile): tcgen05.ld of the S row
+//    half, exact masking (flags, causal token mask, sequence end), online softmax in the
+//    exp2 domain with a lazy rescale of O (only when the running max grows by more than
+//    2^8), P stored to TMEM with tcgen05.st, and the final O / l epilogue.
 //  * Items run (b, h, p)-major so the CTAs in flight share one head's K/V in L2.
 //
 // CUDA-core path: one CTA per query block, fp32 arithmetic, any dtype, block <= 128,
@@ -118,10 +120,9 @@ struct Cfg {
   static constexpr int kQBytes = 128 * D * 2;
   static constexpr int kKBytes = 128 * D * 2;
   static constexpr int kVBytes = 128 * D * 2;
-  static constexpr int kPBytes = 2 * 128 * 128 * 2;  // two P buffers (tile parity)
-  static constexpr int kKStages = D == 128 ? 2 : 4;
-  static constexpr int kVStages = D == 128 ? 2 : 4;
-  static constexpr int kTileBytes = kQBytes + kKStages * kKBytes + kVStages * kVBytes + kPBytes;
+  static constexpr int kKStages = D == 128 ? 3 : 4;
+  static constexpr int kVStages = D == 128 ? 3 : 4;
+  static constexpr int kTileBytes = kQBytes + kKStages * kKBytes + kVStages * kVBytes;
   static constexpr int kXchgBytes = 2 * 2 * 128 * 4;  // partial row maxima [parity][key block][row]
   static constexpr int kAuxBytes = kXchgBytes + 256;   // + mbarriers, TMEM slot, abort flag
   // Tiles start at the first 1024-byte boundary of the dynamic shared memory; the kernel
@@ -129,6 +130,11 @@ struct Cfg {
   static constexpr int kSmemWanted = kTileBytes + kAuxBytes + 1024;
   static constexpr int kSmem = kSmemWanted < 232448 ? kSmemWanted : 232448;
 };
+
+// TMEM columns: S buffers 0-127 and 128-255 (fp32), O 256..256+D-1 (fp32), P buffers
+// 384-447 and 448-511 (128 keys of bf16/f16 packed two per column).
+constexpr uint32_t kTmemO = 256;
+constexpr uint32_t kTmemP = 384;
 
 // Warp 0: TMA producer; warp 1: MMA issuer; warps 2-9: softmax.
 constexpr int kSoftmaxWarps = 8;
@@ -172,13 +178,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sQ = base;
   uint8_t* sK = sQ + C::kQBytes;
   uint8_t* sV = sK + C::kKStages * C::kKBytes;
-  uint8_t* sP = sV + C::kVStages * C::kVBytes;
-  float* xchg = reinterpret_cast<float*>(sP + C::kPBytes);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sP + C::kPBytes + C::kXchgBytes);
+  uint8_t* sEnd = sV + C::kVStages * C::kVBytes;
+  float* xchg = reinterpret_cast<float*>(sEnd);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sEnd + C::kXchgBytes);
   {
     uint32_t dyn;
     asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
-    if (sP + C::kPBytes + C::kAuxBytes > smem_raw + dyn) {
+    if (sEnd + C::kAuxBytes > smem_raw + dyn) {
       if (threadIdx.x == 0) atomicOr(&g_device_status, CAB_DEVICE_LAYOUT);
       return;  // shared memory base not aligned as expected: nothing was touched
     }
@@ -220,7 +226,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_o = tmem + 256;
+  const uint32_t tmem_o = tmem + kTmemO;
   const int G = p.Hq / p.Hkv;
 
   if (warp == 0) {
@@ -274,7 +280,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_f16(128, 128, kBF16 ? 1 : 0, 0, 0);
       constexpr uint32_t idesc_o = make_idesc_f16(128, D, kBF16 ? 1 : 0, 0, 1);
-      const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
+      const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
       uint32_t gi = 0, kt = 0, vt = 0, gt = 0;
       bool ok = true;
       for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
@@ -308,14 +314,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             if (t == 1 && gi > 0 && !mbar_wait(o_free, (gi - 1) & 1, abort_flag)) { ok = false; break; }
             tc_fence_after_sync();
             const uint32_t vb = aV + vs * C::kVBytes;
-            const uint32_t pb = aP + (g & 1) * (C::kPBytes / 2);  // P buffer of this tile
+            const uint32_t pt = tmem + kTmemP + (g & 1) * 64;  // P of this tile, in TMEM
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-              const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-              mma_f16_ss(tmem_o, make_smem_desc(pb + aoff, 16, 1024, 2),
-                         make_smem_desc(vb + kk * 2048, 16384, 1024, 2), idesc_o,
+            for (int kk = 0; kk < 8; ++kk)
+              mma_f16_ts(tmem_o, pt + kk * 8, make_smem_desc(vb + kk * 2048, 16384, 1024, 2), idesc_o,
                          (t > 1 || kk > 0) ? 1u : 0u);
-            }
             mma_commit(&v_empty[vs]);
             mma_commit(o_ready);
             ++vt;
@@ -344,7 +347,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int half = r >> 6;
     const int pair_bar = 1 + quad;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-    uint8_t* prow = sP + kb * 16384 + r * 128;
     constexpr int kHalfD = D / 2;
     uint32_t gt = 0;
     for (int64_t item = blockIdx.x; item < p.items; item += gridDim.x) {
@@ -419,46 +421,49 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           m_run = m_tile;
           l *= alpha;
         }
-        // P of this tile goes to buffer g & 1. That buffer was last read by PV(g - 2),
-        // which completed before S(g) did (one issuing thread, in-order tensor pipe), so
-        // it is free now. Eight keys at a time: exp2 -> pack -> one 16-byte store.
-        uint8_t* pdst = prow + (g & 1) * (C::kPBytes / 2);
+        // P of this tile goes to TMEM buffer g & 1 (this thread: row r, keys 64*kb..+63
+        // -> 32 packed columns). The buffer was last read by PV(g - 2), which completed
+        // before S(g) did (one issuing thread, in-order tensor pipe), so it is free now.
+        const uint32_t pcol = tmem + lane_addr + kTmemP + (g & 1) * 64 + kb * 32;
         float ls[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
         if (all_full) {
           const float nm = -m_run;
 #pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
-            uint32_t w[4];
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t w[16];
 #pragma unroll
-            for (int y = 0; y < 4; ++y) {
-              const int c = 8 * cc + 2 * y;
+            for (int y = 0; y < 16; ++y) {
+              const int c = 32 * hh + 2 * y;
               const float p0 = ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, nm));
               const float p1 = ex2(fmaf(__uint_as_float(s[c + 1]), p.scale_log2, nm));
-              ls[y] += p0 + p1;
+              ls[y & 3] += p0 + p1;
               w[y] = pack2<kBF16>(p0, p1);
             }
-            *reinterpret_cast<uint4*>(pdst + ((cc ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            tmem_st16(pcol + 16 * hh, w);
           }
         } else if (any_live) {
           const bool live = m_run != -INFINITY;
 #pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
-            uint32_t w[4];
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t w[16];
 #pragma unroll
-            for (int y = 0; y < 4; ++y) {
-              const int c = 8 * cc + 2 * y;
+            for (int y = 0; y < 16; ++y) {
+              const int c = 32 * hh + 2 * y;
               const float p0 = (c < lim && live) ? ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, -m_run)) : 0.f;
               const float p1 = (c + 1 < lim && live) ? ex2(fmaf(__uint_as_float(s[c + 1]), p.scale_log2, -m_run)) : 0.f;
-              ls[y] += p0 + p1;
+              ls[y & 3] += p0 + p1;
               w[y] = pack2<kBF16>(p0, p1);
             }
-            *reinterpret_cast<uint4*>(pdst + ((cc ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            tmem_st16(pcol + 16 * hh, w);
           }
         } else {
+          uint32_t w[16];
 #pragma unroll
-          for (int cc = 0; cc < 8; ++cc)
-            *reinterpret_cast<uint4*>(pdst + ((cc ^ (r & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+          for (int y = 0; y < 16; ++y) w[y] = 0u;
+          tmem_st16(pcol, w);
+          tmem_st16(pcol + 16, w);
         }
+        tmem_wait_st();
         l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
 
         // O may only be rescaled once PV(g - 1) has finished accumulating into it. The
@@ -480,7 +485,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
           tmem_wait_st();
         }
-        fence_proxy_async_smem();
         tc_fence_before_sync();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full);
