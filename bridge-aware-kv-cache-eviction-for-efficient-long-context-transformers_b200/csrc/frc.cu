@@ -283,6 +283,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
+      const uint64_t desc_a = make_smem_desc(smem_u32(smem), 16, 1024, 2);
+      const uint64_t desc_b = (kMode == kAffinity) ? make_smem_desc(smem_u32(smem + kABytes), 16, 1024, 2)
+                                                   : make_smem_desc(smem_u32(smem + kABytes), kTileK * 128, 1024, 2);
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) { ok = false; break; }
         tc_fence_after_sync();
@@ -290,13 +293,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int it = 0; it < kiters; ++it) {
           if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
           tc_fence_after_sync();
-          const uint32_t sa = smem_u32(smem + stage * kStageBytes);
-          const uint32_t sb = sa + kABytes;
+          const uint64_t soff = static_cast<uint64_t>((stage * kStageBytes) >> 4);
+          const uint64_t da0 = desc_a + soff, db0 = desc_b + soff;
 #pragma unroll
           for (int kk = 0; kk < kTileK / 16; ++kk) {
-            const uint64_t da = make_smem_desc(sa + kk * 32, 16, 1024, 2);
-            const uint64_t db = (kMode == kAffinity) ? make_smem_desc(sb + kk * 32, 16, 1024, 2)
-                                                     : make_smem_desc(sb + kk * 2048, kTileK * 128, 1024, 2);
+            // advance only the 16-byte-unit start address: 32 B per K step (K-major), 16
+            // rows x 128 B per K step (MN-major B)
+            const uint64_t da = da0 + static_cast<uint64_t>(kk * (32 >> 4));
+            const uint64_t db = db0 + static_cast<uint64_t>(kMode == kAffinity ? kk * (32 >> 4) : kk * (2048 >> 4));
             mma_f16_ss(d_tmem, da, db, idesc, (it > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit(&empty[stage]);

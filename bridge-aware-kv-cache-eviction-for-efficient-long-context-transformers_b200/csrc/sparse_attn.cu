@@ -49,6 +49,12 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // ------------------------------------------------------------------ pair union lists
 struct UnionParams {
   const int32_t* kv_idx;
@@ -280,7 +286,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_f16(128, 128, kBF16 ? 1 : 0, 0, 0);
       constexpr uint32_t idesc_o = make_idesc_f16(128, D, kBF16 ? 1 : 0, 0, 1);
-      const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
+      // Descriptors are built once; per stage and K step only the 14-bit start-address
+      // field (16-byte units, shared memory < 256 KB so it never carries) is advanced.
+      const uint64_t dQ = make_smem_desc(smem_u32(sQ), 16, 1024, 2);
+      const uint64_t dK = make_smem_desc(smem_u32(sK), 16, 1024, 2);
+      const uint64_t dV = make_smem_desc(smem_u32(sV), 16384, 1024, 2);
       uint32_t gi = 0, kt = 0, vt = 0, gt = 0;
       bool ok = true;
       for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
@@ -295,12 +305,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             if (!mbar_wait(&s_free[buf], ((g >> 1) & 1) ^ 1, abort_flag) ||
                 !mbar_wait(&k_full[ks], (kt / C::kKStages) & 1, abort_flag)) { ok = false; break; }
             tc_fence_after_sync();
-            const uint32_t kb = aK + ks * C::kKBytes;
+            const uint64_t dk = dK + static_cast<uint64_t>((ks * C::kKBytes) >> 4);
+            const uint32_t d_s = tmem + buf * 128;
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
-              const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-              mma_f16_ss(tmem + buf * 128, make_smem_desc(aQ + off, 16, 1024, 2),
-                         make_smem_desc(kb + off, 16, 1024, 2), idesc_s, kk > 0 ? 1u : 0u);
+              constexpr uint32_t kAtomStep = 16384 >> 4, kKStep = 32 >> 4;
+              const uint64_t off = (kk >> 2) * kAtomStep + (kk & 3) * kKStep;
+              mma_f16_ss(d_s, dQ + off, dk + off, idesc_s, kk > 0 ? 1u : 0u);
             }
             mma_commit(&k_empty[ks]);
             mma_commit(&s_full[buf]);
@@ -313,11 +324,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 !mbar_wait(&v_full[vs], (vt / C::kVStages) & 1, abort_flag)) { ok = false; break; }
             if (t == 1 && gi > 0 && !mbar_wait(o_free, (gi - 1) & 1, abort_flag)) { ok = false; break; }
             tc_fence_after_sync();
-            const uint32_t vb = aV + vs * C::kVBytes;
+            const uint64_t dv = dV + static_cast<uint64_t>((vs * C::kVBytes) >> 4);
             const uint32_t pt = tmem + kTmemP + (g & 1) * 64;  // P of this tile, in TMEM
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk)
-              mma_f16_ts(tmem_o, pt + kk * 8, make_smem_desc(vb + kk * 2048, 16384, 1024, 2), idesc_o,
+              mma_f16_ts(tmem_o, pt + kk * 8, dv + static_cast<uint64_t>(kk * (2048 >> 4)), idesc_o,
                          (t > 1 || kk > 0) ? 1u : 0u);
             mma_commit(&v_empty[vs]);
             mma_commit(o_ready);
@@ -399,7 +410,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int u = 0; u < 8; ++u) mx8[u] = -INFINITY;
         if (all_full) {
 #pragma unroll
-          for (int c = 0; c < 64; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(s[c]));
+          for (int c = 0; c < 64; c += 2)
+            mx8[(c >> 1) & 7] = fmax3(mx8[(c >> 1) & 7], __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
         } else if (any_live) {
 #pragma unroll
           for (int c = 0; c < 64; ++c)
