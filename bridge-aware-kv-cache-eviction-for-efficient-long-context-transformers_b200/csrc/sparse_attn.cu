@@ -6,17 +6,19 @@
 //    `pair_union_kernel` into one ascending list whose entries carry two flags (kept by
 //    block 2p / by block 2p+1); key blocks are consumed two at a time (a 128-key tile).
 //    A block kept by only one of the two query blocks is masked for the other 64 rows.
-//  * Warp 0 streams Q (once per item), K and V tiles with TMA (128-byte swizzle) into
-//    3-stage (D=128) or 4-stage (D=64) shared-memory rings. One thread of warp 1 issues
-//    S = Q K^T (M=128, N=128, K=D, both operands in shared memory) into one of two TMEM
-//    S buffers and, one tile behind, O += P V with P read from TMEM and V read MN-major
-//    from its natural [keys, D] layout (M=128, N=D, K=128), so S(t+1) overlaps the
-//    softmax of t and P never touches shared memory (whose bandwidth the tensor core,
-//    TMA and softmax would otherwise share).
+//  * Warp 0 streams K and V tiles with TMA (128-byte swizzle) into 4/3-stage (D=128) or
+//    6/6-stage (D=64) shared-memory rings. The softmax warps write each item's Q rows
+//    into TMEM. One thread of warp 1 issues S = Q K^T (M=128, N=128, K=D; Q from TMEM, K
+//    from shared memory) into one of two TMEM S buffers and, one tile behind,
+//    O += P V (P from TMEM, V read MN-major from its natural [keys, D] layout; M=128,
+//    N=D, K=128), so S(t+1) overlaps the softmax of t. Only K and V are ever read from
+//    shared memory by the tensor core, which keeps its operand traffic well inside the
+//    shared-memory bandwidth that it also shares with the TMA writes.
 //  * Warps 2-9, two per row (one per 64-key block of the tile): tcgen05.ld of the S row
 //    half, exact masking (flags, causal token mask, sequence end), online softmax in the
 //    exp2 domain with a lazy rescale of O (only when the running max grows by more than
-//    2^8), P stored to TMEM with tcgen05.st, and the final O / l epilogue.
+//    2^8), P stored to TMEM over the S columns it came from, and the final O / l
+//    epilogue.
 //  * Items run (b, h, p)-major so the CTAs in flight share one head's K/V in L2.
 //
 // CUDA-core path: one CTA per query block, fp32 arithmetic, any dtype, block <= 128,
@@ -123,32 +125,38 @@ __global__ void __launch_bounds__(128) pair_union_kernel(const UnionParams p) {
 template <int D>
 struct Cfg {
   static constexpr int kAtoms = D / 64;
-  static constexpr int kQBytes = 128 * D * 2;
-  static constexpr int kKBytes = 128 * D * 2;
+  static constexpr int kKBytes = 128 * D * 2;  // one tile = two 64-key blocks
   static constexpr int kVBytes = 128 * D * 2;
-  static constexpr int kKStages = D == 128 ? 3 : 4;
-  static constexpr int kVStages = D == 128 ? 3 : 4;
-  static constexpr int kTileBytes = kQBytes + kKStages * kKBytes + kVStages * kVBytes;
-  static constexpr int kXchgBytes = 2 * 2 * 128 * 4;  // partial row maxima [parity][key block][row]
-  static constexpr int kAuxBytes = kXchgBytes + 256;   // + mbarriers, TMEM slot, abort flag
+  static constexpr int kKStages = D == 128 ? 4 : 6;
+  static constexpr int kVStages = D == 128 ? 3 : 6;
+  static constexpr int kTileBytes = kKStages * kKBytes + kVStages * kVBytes;
+  static constexpr int kXchgBytes = 2 * 2 * 128 * 4;  // row-max / row-sum exchange [parity][kb][row]
+  static constexpr int kAuxBytes = kXchgBytes + 512;   // + mbarriers (<= 62), TMEM slot, abort flag
   // Tiles start at the first 1024-byte boundary of the dynamic shared memory; the kernel
   // checks at run time that tiles + aux fit in what it was given.
   static constexpr int kSmemWanted = kTileBytes + kAuxBytes + 1024;
   static constexpr int kSmem = kSmemWanted < 232448 ? kSmemWanted : 232448;
 };
 
-// TMEM columns: S buffers 0-127 and 128-255 (fp32), O 256..256+D-1 (fp32), P buffers
-// 384-447 and 448-511 (128 keys of bf16/f16 packed two per column).
+// TMEM columns: S buffers 0-127 and 128-255 (fp32; the P of a tile overwrites the S
+// columns it came from: the thread owning keys 64*kb..+63 of a row writes their 32 packed
+// columns at S column 64*kb), O 256..256+D-1 (fp32), Q 384..384+D/2-1 (bf16/f16 packed
+// two per column, row r in lane r: the A operand of S = Q K^T).
 constexpr uint32_t kTmemO = 256;
-constexpr uint32_t kTmemP = 384;
+constexpr uint32_t kTmemQ = 384;
 
-// Warp 0: TMA producer; warp 1: MMA issuer; warps 2-9: softmax.
+// Warp 0: TMA producer; warp 1: issues S = Q K^T; warps 2-9: softmax; warp 10: issues
+// O += P V. Two issuing threads keep the tensor pipe queued: while one blocks on a full
+// MMA queue, the other's group is already waiting behind it.
 constexpr int kSoftmaxWarps = 8;
-constexpr int kAttnThreads = 64 + 32 * kSoftmaxWarps;
+constexpr int kPvWarp = 2 + kSoftmaxWarps;
+constexpr int kAttnThreads = 32 * (kPvWarp + 1);
 
 struct Params {
   int32_t B, Hq, Hkv, N, M, P;
   int64_t items;
+  const void* q;
+  int64_t q_s0, q_s1, q_s2;
   int64_t o_s0, o_s1, o_s2;
   void* out;
   float* lse;
@@ -176,13 +184,12 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 
 template <int D, bool kBF16>
 __global__ void __launch_bounds__(kAttnThreads, 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-                   const __grid_constant__ CUtensorMap vmap, const Params p) {
+    attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                   const Params p) {
   using C = Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = base;
-  uint8_t* sK = sQ + C::kQBytes;
+  uint8_t* sK = base;
   uint8_t* sV = sK + C::kKStages * C::kKBytes;
   uint8_t* sEnd = sV + C::kVStages * C::kVBytes;
   float* xchg = reinterpret_cast<float*>(sEnd);
@@ -196,34 +203,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   }
   uint64_t* q_full = bar;
-  uint64_t* q_empty = bar + 1;
-  uint64_t* k_full = bar + 2;
+  uint64_t* k_full = bar + 1;
   uint64_t* k_empty = k_full + C::kKStages;
   uint64_t* v_full = k_empty + C::kKStages;
   uint64_t* v_empty = v_full + C::kVStages;
   uint64_t* s_full = v_empty + C::kVStages;
-  uint64_t* s_free = s_full + 2;
-  uint64_t* p_full = s_free + 2;
+  uint64_t* buf_free = s_full + 2;  // S/P buffer reusable: PV of its last tile completed
+  uint64_t* p_full = buf_free + 2;
   uint64_t* o_ready = p_full + 1;
   uint64_t* o_free = o_ready + 1;
-  uint64_t* drain = o_free + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* drain = o_free + 1;     // [0] S issuer, [1] PV issuer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    prefetch_tensormap(&qmap);
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
+    mbar_init(q_full, kSoftmaxWarps);
     for (int s = 0; s < C::kKStages; ++s) { mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1); }
     for (int s = 0; s < C::kVStages; ++s) { mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1); }
-    for (int s = 0; s < 2; ++s) { mbar_init(&s_full[s], 1); mbar_init(&s_free[s], kSoftmaxWarps); }
+    for (int s = 0; s < 2; ++s) { mbar_init(&s_full[s], 1); mbar_init(&buf_free[s], 1); }
     mbar_init(p_full, kSoftmaxWarps);
     mbar_init(o_ready, 1);
     mbar_init(o_free, kSoftmaxWarps);
-    mbar_init(drain, 1);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -233,23 +238,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_after_sync();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tmem_o = tmem + kTmemO;
+  const uint32_t tmem_q = tmem + kTmemQ;
   const int G = p.Hq / p.Hkv;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ TMA producer (K, V)
     if (lane == 0) {
-      uint32_t gi = 0, kt = 0, vt = 0;
+      uint32_t kt = 0, vt = 0;
       bool ok = true;
       for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
         const int T = p.ntiles[item];
         if (T == 0) continue;
-        const int bh = static_cast<int>(item / p.P), pr = static_cast<int>(item % p.P);
-        const int b = bh / p.Hq, h = bh % p.Hq, hk = h / G;
+        const int bh = static_cast<int>(item / p.P);
+        const int b = bh / p.Hq, hk = (bh % p.Hq) / G;
         const uint32_t* ul = p.ulist + item * p.stride;
-        if (!mbar_wait(q_empty, (gi & 1) ^ 1, abort_flag)) { ok = false; break; }
-        mbar_arrive_expect_tx(q_full, C::kQBytes);
-#pragma unroll
-        for (int a = 0; a < C::kAtoms; ++a) tma_load_4d(sQ + a * 16384, &qmap, q_full, 64 * a, 128 * pr, h, b);
         for (int t = 0; t < T; ++t) {
           const int j0 = static_cast<int>(ul[2 * t] & kIdxMask), j1 = static_cast<int>(ul[2 * t + 1] & kIdxMask);
           const int ks = kt % C::kKStages;
@@ -273,85 +275,102 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
           ++vt;
         }
-        ++gi;
       }
       if (!ok) {
         // bounded drain of the loads this thread may still have in flight
-        (void)mbar_wait(q_full, (gi & 1), nullptr);
+        for (int s = 0; s < C::kKStages; ++s) (void)mbar_wait(&k_full[s], ((kt + s) / C::kKStages) & 1, nullptr);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------ S = Q K^T issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_f16(128, 128, kBF16 ? 1 : 0, 0, 0);
-      constexpr uint32_t idesc_o = make_idesc_f16(128, D, kBF16 ? 1 : 0, 0, 1);
       // Descriptors are built once; per stage and K step only the 14-bit start-address
       // field (16-byte units, shared memory < 256 KB so it never carries) is advanced.
-      const uint64_t dQ = make_smem_desc(smem_u32(sQ), 16, 1024, 2);
       const uint64_t dK = make_smem_desc(smem_u32(sK), 16, 1024, 2);
-      const uint64_t dV = make_smem_desc(smem_u32(sV), 16384, 1024, 2);
-      uint32_t gi = 0, kt = 0, vt = 0, gt = 0;
+      uint32_t gi = 0, kt = 0, gt = 0;
       bool ok = true;
       for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
         const int T = p.ntiles[item];
         if (T == 0) continue;
         if (!mbar_wait(q_full, gi & 1, abort_flag)) { ok = false; break; }
         tc_fence_after_sync();
-        for (int t = 0; t <= T && ok; ++t) {
-          if (t < T) {
-            const uint32_t g = gt + t, buf = g & 1;
-            const int ks = kt % C::kKStages;
-            if (!mbar_wait(&s_free[buf], ((g >> 1) & 1) ^ 1, abort_flag) ||
-                !mbar_wait(&k_full[ks], (kt / C::kKStages) & 1, abort_flag)) { ok = false; break; }
-            tc_fence_after_sync();
-            const uint64_t dk = dK + static_cast<uint64_t>((ks * C::kKBytes) >> 4);
-            const uint32_t d_s = tmem + buf * 128;
+        for (int t = 0; t < T; ++t) {
+          // S(g) = Q K(g)^T into buffer g & 1 once PV(g - 2) (which read P(g - 2) there)
+          // has completed; Q from TMEM, K from shared memory (K-major)
+          const uint32_t g = gt + t, buf = g & 1;
+          const int ks = kt % C::kKStages;
+          if (!mbar_wait(&buf_free[buf], ((g >> 1) & 1) ^ 1, abort_flag) ||
+              !mbar_wait(&k_full[ks], (kt / C::kKStages) & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after_sync();
+          const uint64_t dk = dK + static_cast<uint64_t>((ks * C::kKBytes) >> 4);
+          const uint32_t d_s = tmem + buf * 128;
 #pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              constexpr uint32_t kAtomStep = 16384 >> 4, kKStep = 32 >> 4;
-              const uint64_t off = (kk >> 2) * kAtomStep + (kk & 3) * kKStep;
-              mma_f16_ss(d_s, dQ + off, dk + off, idesc_s, kk > 0 ? 1u : 0u);
-            }
-            mma_commit(&k_empty[ks]);
-            mma_commit(&s_full[buf]);
-            ++kt;
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t off = (kk >> 2) * (16384 >> 4) + (kk & 3) * (32 >> 4);
+            mma_f16_ts(d_s, tmem_q + kk * 8, dk + off, idesc_s, kk > 0 ? 1u : 0u);
           }
-          if (t >= 1) {
-            const uint32_t g = gt + t - 1;
-            const int vs = vt % C::kVStages;
-            if (!mbar_wait(p_full, g & 1, abort_flag) ||
-                !mbar_wait(&v_full[vs], (vt / C::kVStages) & 1, abort_flag)) { ok = false; break; }
-            if (t == 1 && gi > 0 && !mbar_wait(o_free, (gi - 1) & 1, abort_flag)) { ok = false; break; }
-            tc_fence_after_sync();
-            const uint64_t dv = dV + static_cast<uint64_t>((vs * C::kVBytes) >> 4);
-            const uint32_t pt = tmem + kTmemP + (g & 1) * 64;  // P of this tile, in TMEM
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              mma_f16_ts(tmem_o, pt + kk * 8, dv + static_cast<uint64_t>(kk * (2048 >> 4)), idesc_o,
-                         (t > 1 || kk > 0) ? 1u : 0u);
-            mma_commit(&v_empty[vs]);
-            mma_commit(o_ready);
-            ++vt;
-          }
+          mma_commit(&k_empty[ks]);
+          mma_commit(&s_full[buf]);
+          ++kt;
         }
         if (!ok) break;
-        mma_commit(q_empty);
         gt += T;
         ++gi;
       }
-      if (gi > 0 || gt > 0) {
-        mma_commit(drain);
-        (void)mbar_wait(drain, 0, nullptr);
+      if (gi > 0) {
+        mma_commit(&drain[0]);
+        (void)mbar_wait(&drain[0], 0, nullptr);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kPvWarp) {
+    // ------------------------------------------------------------ O += P V issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_o = make_idesc_f16(128, D, kBF16 ? 1 : 0, 0, 1);
+      const uint64_t dV = make_smem_desc(smem_u32(sV), 16384, 1024, 2);
+      uint32_t gi = 0, vt = 0, gt = 0;
+      bool ok = true;
+      for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
+        const int T = p.ntiles[item];
+        if (T == 0) continue;
+        for (int t = 0; t < T; ++t) {
+          // P from TMEM (in its S buffer), V from shared memory (MN-major)
+          const uint32_t g = gt + t;
+          const int vs = vt % C::kVStages;
+          if (!mbar_wait(p_full, g & 1, abort_flag) ||
+              !mbar_wait(&v_full[vs], (vt / C::kVStages) & 1, abort_flag)) { ok = false; break; }
+          if (t == 0 && gi > 0 && !mbar_wait(o_free, (gi - 1) & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after_sync();
+          const uint64_t dv = dV + static_cast<uint64_t>((vs * C::kVBytes) >> 4);
+          const uint32_t pt = tmem + (g & 1) * 128;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_f16_ts(tmem_o, pt + (kk >> 2) * 64 + (kk & 3) * 8,
+                       dv + static_cast<uint64_t>(kk * (2048 >> 4)), idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&v_empty[vs]);
+          mma_commit(o_ready);
+          mma_commit(&buf_free[g & 1]);
+          ++vt;
+        }
+        if (!ok) break;
+        gt += T;
+        ++gi;
+      }
+      if (gi > 0) {
+        mma_commit(&drain[1]);
+        (void)mbar_wait(&drain[1], 0, nullptr);
       }
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax + epilogue
+    // (warps 2 .. kPvWarp - 1)
     // Warp w (2..9) owns TMEM lane quadrant w & 3 (rows 32*(w&3) .. +31 of the 128-row
     // tile) and key block kb = (w - 2) / 4 of every 128-key tile (columns 64*kb .. +63).
-    // The two threads holding the two halves of a row swap partial row maxima through
-    // shared memory (double-buffered by tile parity) under a 64-thread named barrier.
+    // The two threads of a row swap partial row maxima through shared memory
+    // (double-buffered by tile parity) under a 64-thread named barrier.
     const int quad = warp & 3;
     const int kb = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
@@ -359,6 +378,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int pair_bar = 1 + quad;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     constexpr int kHalfD = D / 2;
+    using InT = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
     uint32_t gt = 0;
     for (int64_t item = blockIdx.x; item < p.items; item += gridDim.x) {
       const int T = p.ntiles[item];
@@ -366,8 +386,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int b = bh / p.Hq, h = bh % p.Hq;
       const int row = 128 * pr + r;
       const int64_t ooff = b * p.o_s0 + h * p.o_s1 + static_cast<int64_t>(row) * p.o_s2;
-      using OutT = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
-      OutT* orow = reinterpret_cast<OutT*>(p.out) + ooff + kb * kHalfD;
+      InT* orow = reinterpret_cast<InT*>(p.out) + ooff + kb * kHalfD;
       if (T == 0) {
         if (row < p.N) {
 #pragma unroll
@@ -375,6 +394,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (p.lse && kb == 0) p.lse[static_cast<int64_t>(bh) * p.N + row] = -INFINITY;
         }
         continue;
+      }
+      // ---- Q rows of this item -> TMEM (row r in lane r, D/2 elements per thread).
+      // Every S MMA of the previous item has completed: this thread waited for the last
+      // one's s_full before leaving that item.
+      {
+        const InT* qrow = reinterpret_cast<const InT*>(p.q) + b * p.q_s0 + h * p.q_s1 +
+                          static_cast<int64_t>(row) * p.q_s2 + kb * kHalfD;
+#pragma unroll
+        for (int c = 0; c < kHalfD; c += 32) {
+          uint32_t w[16];
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            const uint4 v = row < p.N ? __ldg(reinterpret_cast<const uint4*>(qrow + c) + x) : make_uint4(0, 0, 0, 0);
+            w[4 * x] = v.x; w[4 * x + 1] = v.y; w[4 * x + 2] = v.z; w[4 * x + 3] = v.w;
+          }
+          tmem_st16(tmem_q + lane_addr + kb * (kHalfD / 2) + c / 2, w);
+        }
+        tmem_wait_st();
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(q_full);
       }
       const uint32_t* ul = p.ulist + item * p.stride;
       float m_run = -INFINITY, l = 0.f;
@@ -390,20 +430,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         lim = max(lim, 0);
         const bool any_live = __any_sync(0xffffffffu, lim > 0);
         const bool all_full = __all_sync(0xffffffffu, lim >= 64);
+        const uint32_t scol = tmem + lane_addr + buf * 128 + kb * 64;  // S in, P out
 
         const bool okw = mbar_wait(&s_full[buf], (g >> 1) & 1, abort_flag);
         if (!__all_sync(0xffffffffu, okw)) { ok = false; break; }
         tc_fence_after_sync();
         uint32_t s[64];
         if (any_live) {
-          tmem_ld32(tmem + lane_addr + buf * 128 + kb * 64, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-          tmem_ld32(tmem + lane_addr + buf * 128 + kb * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+          tmem_ld32(scol, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+          tmem_ld32(scol + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
           tmem_wait_ld();
         }
-        tc_fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[buf]);
-
         // row max over this thread's 64 keys: eight independent chains, then a tree
         float mx8[8];
 #pragma unroll
@@ -433,10 +470,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           m_run = m_tile;
           l *= alpha;
         }
-        // P of this tile goes to TMEM buffer g & 1 (this thread: row r, keys 64*kb..+63
-        // -> 32 packed columns). The buffer was last read by PV(g - 2), which completed
-        // before S(g) did (one issuing thread, in-order tensor pipe), so it is free now.
-        const uint32_t pcol = tmem + lane_addr + kTmemP + (g & 1) * 64 + kb * 32;
+        // P overwrites this thread's own S columns (already in registers). The previous
+        // reader of this buffer, PV(g - 2), completed before S(g) did (one issuing
+        // thread, in-order tensor pipe).
         float ls[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
         if (all_full) {
           const float nm = -m_run;
@@ -451,7 +487,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               ls[y & 3] += p0 + p1;
               w[y] = pack2<kBF16>(p0, p1);
             }
-            tmem_st16(pcol + 16 * hh, w);
+            tmem_st16(scol + 16 * hh, w);
           }
         } else if (any_live) {
           const bool live = m_run != -INFINITY;
@@ -466,14 +502,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               ls[y & 3] += p0 + p1;
               w[y] = pack2<kBF16>(p0, p1);
             }
-            tmem_st16(pcol + 16 * hh, w);
+            tmem_st16(scol + 16 * hh, w);
           }
         } else {
           uint32_t w[16];
 #pragma unroll
           for (int y = 0; y < 16; ++y) w[y] = 0u;
-          tmem_st16(pcol, w);
-          tmem_st16(pcol + 16, w);
+          tmem_st16(scol, w);
+          tmem_st16(scol + 16, w);
         }
         tmem_wait_st();
         l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
@@ -521,19 +557,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (row < p.N) {
 #pragma unroll
           for (int x = 0; x < 16; x += 8) {
-            uint32_t w[4];
+            uint32_t wv[4];
 #pragma unroll
-            for (int y = 0; y < 4; ++y) {
-              const float a0 = __uint_as_float(o[x + 2 * y]) * inv, a1 = __uint_as_float(o[x + 2 * y + 1]) * inv;
-              if constexpr (kBF16) {
-                __nv_bfloat162 v2 = __floats2bfloat162_rn(a0, a1);
-                w[y] = *reinterpret_cast<uint32_t*>(&v2);
-              } else {
-                __half2 v2 = __floats2half2_rn(a0, a1);
-                w[y] = *reinterpret_cast<uint32_t*>(&v2);
-              }
-            }
-            *reinterpret_cast<uint4*>(orow + c + x) = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int y = 0; y < 4; ++y)
+              wv[y] = pack2<kBF16>(__uint_as_float(o[x + 2 * y]) * inv, __uint_as_float(o[x + 2 * y + 1]) * inv);
+            *reinterpret_cast<uint4*>(orow + c + x) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
           }
         }
       }
@@ -668,12 +696,11 @@ static bool use_tensor_cores(int dtype, int64_t D, int64_t bs) {
 }
 
 template <int D, bool kBF16>
-static int launch_tc(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const Params& p,
-                     cudaStream_t st) {
+static int launch_tc(const CUtensorMap& km, const CUtensorMap& vm, const Params& p, cudaStream_t st) {
   auto kern = attn_tc_kernel<D, kBF16>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::kSmem);
   const int grid = static_cast<int>(std::min<int64_t>(p.items, current_sm_count()));
-  kern<<<grid, kAttnThreads, Cfg<D>::kSmem, st>>>(qm, km, vm, p);
+  kern<<<grid, kAttnThreads, Cfg<D>::kSmem, st>>>(km, vm, p);
   return check_launch("attn_tc_kernel");
 }
 
@@ -742,14 +769,13 @@ extern "C" int cab_sparse_attn_fwd(const void* q, const void* k, const void* v, 
     pair_union_kernel<<<ugrid, 128, usmem, st>>>(up);
     if (int rc = check_launch("pair_union_kernel")) return rc;
 
-    CUtensorMap qm{}, km{}, vm{};
+    CUtensorMap km{}, vm{};
     auto mk = [&](CUtensorMap* m, const void* ptr, int64_t H, const int64_t* s, uint32_t rows) {
       uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(N), static_cast<uint64_t>(H), static_cast<uint64_t>(B)};
       uint64_t str[3] = {static_cast<uint64_t>(s[2]) * es, static_cast<uint64_t>(s[1]) * es, static_cast<uint64_t>(s[0]) * es};
       uint32_t box[4] = {64, rows, 1, 1};
       return make_tensor_map(m, tma_type(dtype), 4, ptr, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
     };
-    if (int rc = mk(&qm, q, Hq, q_strides, 128)) return rc;
     if (int rc = mk(&km, k, Hkv, k_strides, 64)) return rc;
     if (int rc = mk(&vm, v, Hkv, v_strides, 64)) return rc;
     Params p{};
@@ -760,6 +786,10 @@ extern "C" int cab_sparse_attn_fwd(const void* q, const void* k, const void* v, 
     p.M = static_cast<int32_t>(M);
     p.P = up.P;
     p.items = L.items;
+    p.q = q;
+    p.q_s0 = q_strides[0];
+    p.q_s1 = q_strides[1];
+    p.q_s2 = q_strides[2];
     p.o_s0 = o_strides[0];
     p.o_s1 = o_strides[1];
     p.o_s2 = o_strides[2];
@@ -771,8 +801,8 @@ extern "C" int cab_sparse_attn_fwd(const void* q, const void* k, const void* v, 
     p.scale_log2 = softmax_scale * kLog2e;
     p.causal = causal != 0;
     const bool bf = dtype == CAB_DTYPE_BF16;
-    if (D == 128) return bf ? launch_tc<128, true>(qm, km, vm, p, st) : launch_tc<128, false>(qm, km, vm, p, st);
-    return bf ? launch_tc<64, true>(qm, km, vm, p, st) : launch_tc<64, false>(qm, km, vm, p, st);
+    if (D == 128) return bf ? launch_tc<128, true>(km, vm, p, st) : launch_tc<128, false>(km, vm, p, st);
+    return bf ? launch_tc<64, true>(km, vm, p, st) : launch_tc<64, false>(km, vm, p, st);
   }
 
   if (block_size > 128 || D > 128)
