@@ -125,11 +125,12 @@ __global__ void __launch_bounds__(128) pair_union_kernel(const UnionParams p) {
 template <int D>
 struct Cfg {
   static constexpr int kAtoms = D / 64;
+  static constexpr int kQBytes = 128 * D * 2;
   static constexpr int kKBytes = 128 * D * 2;  // one tile = two 64-key blocks
   static constexpr int kVBytes = 128 * D * 2;
-  static constexpr int kKStages = D == 128 ? 4 : 6;
-  static constexpr int kVStages = D == 128 ? 3 : 6;
-  static constexpr int kTileBytes = kKStages * kKBytes + kVStages * kVBytes;
+  static constexpr int kKStages = D == 128 ? 3 : 5;
+  static constexpr int kVStages = D == 128 ? 3 : 5;
+  static constexpr int kTileBytes = kQBytes + kKStages * kKBytes + kVStages * kVBytes;
   static constexpr int kXchgBytes = 2 * 2 * 128 * 4;  // row-max / row-sum exchange [parity][kb][row]
   static constexpr int kAuxBytes = kXchgBytes + 512;   // + mbarriers (<= 62), TMEM slot, abort flag
   // Tiles start at the first 1024-byte boundary of the dynamic shared memory; the kernel
@@ -138,12 +139,12 @@ struct Cfg {
   static constexpr int kSmem = kSmemWanted < 232448 ? kSmemWanted : 232448;
 };
 
-// TMEM columns: S buffers 0-127 and 128-255 (fp32; the P of a tile overwrites the S
+// TMEM columns: three S buffers at 0, 128, 256 (fp32; the P of a tile overwrites the S
 // columns it came from: the thread owning keys 64*kb..+63 of a row writes their 32 packed
-// columns at S column 64*kb), O 256..256+D-1 (fp32), Q 384..384+D/2-1 (bf16/f16 packed
-// two per column, row r in lane r: the A operand of S = Q K^T).
-constexpr uint32_t kTmemO = 256;
-constexpr uint32_t kTmemQ = 384;
+// columns at S column 64*kb), O at 384..384+D-1 (fp32). Three S/P buffers keep three tiles
+// in flight: S(g) may start once PV(g - 3), the last reader of its buffer, has finished.
+constexpr int kSBufs = 3;
+constexpr uint32_t kTmemO = 384;
 
 // Warp 0: TMA producer; warp 1: issues S = Q K^T; warps 2-9: softmax; warp 10: issues
 // O += P V. Two issuing threads keep the tensor pipe queued: while one blocks on a full
@@ -184,12 +185,13 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 
 template <int D, bool kBF16>
 __global__ void __launch_bounds__(kAttnThreads, 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
-                   const Params p) {
+    attn_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                   const __grid_constant__ CUtensorMap vmap, const Params p) {
   using C = Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sK = base;
+  uint8_t* sQ = base;
+  uint8_t* sK = sQ + C::kQBytes;
   uint8_t* sV = sK + C::kKStages * C::kKBytes;
   uint8_t* sEnd = sV + C::kVStages * C::kVBytes;
   float* xchg = reinterpret_cast<float*>(sEnd);
@@ -203,13 +205,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   }
   uint64_t* q_full = bar;
-  uint64_t* k_full = bar + 1;
+  uint64_t* q_empty = bar + 1;
+  uint64_t* k_full = bar + 2;
   uint64_t* k_empty = k_full + C::kKStages;
   uint64_t* v_full = k_empty + C::kKStages;
   uint64_t* v_empty = v_full + C::kVStages;
   uint64_t* s_full = v_empty + C::kVStages;
-  uint64_t* buf_free = s_full + 2;  // S/P buffer reusable: PV of its last tile completed
-  uint64_t* p_full = buf_free + 2;
+  uint64_t* buf_free = s_full + kSBufs;  // S/P buffer reusable: PV of its last tile completed
+  uint64_t* p_full = buf_free + kSBufs;
   uint64_t* o_ready = p_full + 1;
   uint64_t* o_free = o_ready + 1;
   uint64_t* drain = o_free + 1;     // [0] S issuer, [1] PV issuer
@@ -218,12 +221,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
+    prefetch_tensormap(&qmap);
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
-    mbar_init(q_full, kSoftmaxWarps);
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int s = 0; s < C::kKStages; ++s) { mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1); }
     for (int s = 0; s < C::kVStages; ++s) { mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1); }
-    for (int s = 0; s < 2; ++s) { mbar_init(&s_full[s], 1); mbar_init(&buf_free[s], 1); }
+    for (int s = 0; s < kSBufs; ++s) { mbar_init(&s_full[s], 1); mbar_init(&buf_free[s], 1); }
     mbar_init(p_full, kSoftmaxWarps);
     mbar_init(o_ready, 1);
     mbar_init(o_free, kSoftmaxWarps);
@@ -238,20 +243,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_after_sync();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tmem_o = tmem + kTmemO;
-  const uint32_t tmem_q = tmem + kTmemQ;
   const int G = p.Hq / p.Hkv;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer (K, V)
+    // ------------------------------------------------------------ TMA producer (Q, K, V)
     if (lane == 0) {
-      uint32_t kt = 0, vt = 0;
+      uint32_t gi = 0, kt = 0, vt = 0;
       bool ok = true;
       for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
         const int T = p.ntiles[item];
         if (T == 0) continue;
-        const int bh = static_cast<int>(item / p.P);
-        const int b = bh / p.Hq, hk = (bh % p.Hq) / G;
+        const int bh = static_cast<int>(item / p.P), pr = static_cast<int>(item % p.P);
+        const int b = bh / p.Hq, h = bh % p.Hq, hk = h / G;
         const uint32_t* ul = p.ulist + item * p.stride;
+        if (!mbar_wait(q_empty, (gi & 1) ^ 1, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(q_full, C::kQBytes);
+#pragma unroll
+        for (int a = 0; a < C::kAtoms; ++a) tma_load_4d(sQ + a * 16384, &qmap, q_full, 64 * a, 128 * pr, h, b);
+        ++gi;
         for (int t = 0; t < T; ++t) {
           const int j0 = static_cast<int>(ul[2 * t] & kIdxMask), j1 = static_cast<int>(ul[2 * t + 1] & kIdxMask);
           const int ks = kt % C::kKStages;
@@ -288,6 +297,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       constexpr uint32_t idesc_s = make_idesc_f16(128, 128, kBF16 ? 1 : 0, 0, 0);
       // Descriptors are built once; per stage and K step only the 14-bit start-address
       // field (16-byte units, shared memory < 256 KB so it never carries) is advanced.
+      const uint64_t dQ = make_smem_desc(smem_u32(sQ), 16, 1024, 2);
       const uint64_t dK = make_smem_desc(smem_u32(sK), 16, 1024, 2);
       uint32_t gi = 0, kt = 0, gt = 0;
       bool ok = true;
@@ -297,11 +307,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (!mbar_wait(q_full, gi & 1, abort_flag)) { ok = false; break; }
         tc_fence_after_sync();
         for (int t = 0; t < T; ++t) {
-          // S(g) = Q K(g)^T into buffer g & 1 once PV(g - 2) (which read P(g - 2) there)
-          // has completed; Q from TMEM, K from shared memory (K-major)
-          const uint32_t g = gt + t, buf = g & 1;
+          // S(g) = Q K(g)^T into buffer g % 3 once PV(g - 3) (which read P(g - 3) there)
+          // has completed; Q and K from shared memory (K-major)
+          const uint32_t g = gt + t, buf = g % kSBufs;
           const int ks = kt % C::kKStages;
-          if (!mbar_wait(&buf_free[buf], ((g >> 1) & 1) ^ 1, abort_flag) ||
+          if (!mbar_wait(&buf_free[buf], ((g / kSBufs) & 1) ^ 1, abort_flag) ||
               !mbar_wait(&k_full[ks], (kt / C::kKStages) & 1, abort_flag)) { ok = false; break; }
           tc_fence_after_sync();
           const uint64_t dk = dK + static_cast<uint64_t>((ks * C::kKBytes) >> 4);
@@ -309,13 +319,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint64_t off = (kk >> 2) * (16384 >> 4) + (kk & 3) * (32 >> 4);
-            mma_f16_ts(d_s, tmem_q + kk * 8, dk + off, idesc_s, kk > 0 ? 1u : 0u);
+            mma_f16_ss(d_s, dQ + off, dk + off, idesc_s, kk > 0 ? 1u : 0u);
           }
           mma_commit(&k_empty[ks]);
           mma_commit(&s_full[buf]);
           ++kt;
         }
         if (!ok) break;
+        mma_commit(q_empty);
         gt += T;
         ++gi;
       }
@@ -344,14 +355,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (t == 0 && gi > 0 && !mbar_wait(o_free, (gi - 1) & 1, abort_flag)) { ok = false; break; }
           tc_fence_after_sync();
           const uint64_t dv = dV + static_cast<uint64_t>((vs * C::kVBytes) >> 4);
-          const uint32_t pt = tmem + (g & 1) * 128;
+          const uint32_t pt = tmem + (g % kSBufs) * 128;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
             mma_f16_ts(tmem_o, pt + (kk >> 2) * 64 + (kk & 3) * 8,
                        dv + static_cast<uint64_t>(kk * (2048 >> 4)), idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
           mma_commit(&v_empty[vs]);
           mma_commit(o_ready);
-          mma_commit(&buf_free[g & 1]);
+          mma_commit(&buf_free[g % kSBufs]);
           ++vt;
         }
         if (!ok) break;
@@ -395,33 +406,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         continue;
       }
-      // ---- Q rows of this item -> TMEM (row r in lane r, D/2 elements per thread).
-      // Every S MMA of the previous item has completed: this thread waited for the last
-      // one's s_full before leaving that item.
-      {
-        const InT* qrow = reinterpret_cast<const InT*>(p.q) + b * p.q_s0 + h * p.q_s1 +
-                          static_cast<int64_t>(row) * p.q_s2 + kb * kHalfD;
-#pragma unroll
-        for (int c = 0; c < kHalfD; c += 32) {
-          uint32_t w[16];
-#pragma unroll
-          for (int x = 0; x < 4; ++x) {
-            const uint4 v = row < p.N ? __ldg(reinterpret_cast<const uint4*>(qrow + c) + x) : make_uint4(0, 0, 0, 0);
-            w[4 * x] = v.x; w[4 * x + 1] = v.y; w[4 * x + 2] = v.z; w[4 * x + 3] = v.w;
-          }
-          tmem_st16(tmem_q + lane_addr + kb * (kHalfD / 2) + c / 2, w);
-        }
-        tmem_wait_st();
-        tc_fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(q_full);
-      }
       const uint32_t* ul = p.ulist + item * p.stride;
       float m_run = -INFINITY, l = 0.f;
       bool ok = true;
       uint32_t e_next = ul[kb];
       for (int t = 0; t < T; ++t) {
-        const uint32_t g = gt + t, buf = g & 1;
+        const uint32_t g = gt + t, buf = g % kSBufs;
         const uint32_t e = e_next;
         if (t + 1 < T) e_next = ul[2 * (t + 1) + kb];
         const int j = static_cast<int>(e & kIdxMask);
@@ -432,7 +422,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const bool all_full = __all_sync(0xffffffffu, lim >= 64);
         const uint32_t scol = tmem + lane_addr + buf * 128 + kb * 64;  // S in, P out
 
-        const bool okw = mbar_wait(&s_full[buf], (g >> 1) & 1, abort_flag);
+        const bool okw = mbar_wait(&s_full[buf], (g / kSBufs) & 1, abort_flag);
         if (!__all_sync(0xffffffffu, okw)) { ok = false; break; }
         tc_fence_after_sync();
         uint32_t s[64];
@@ -470,9 +460,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           m_run = m_tile;
           l *= alpha;
         }
-        // P overwrites this thread's own S columns (already in registers). The previous
-        // reader of this buffer, PV(g - 2), completed before S(g) did (one issuing
-        // thread, in-order tensor pipe).
+        // P overwrites this thread's own S columns (already in registers); PV(g) reads
+        // it from there, and S(g + 3) waits for that PV before reusing the buffer.
         float ls[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
         if (all_full) {
           const float nm = -m_run;
@@ -696,11 +685,12 @@ static bool use_tensor_cores(int dtype, int64_t D, int64_t bs) {
 }
 
 template <int D, bool kBF16>
-static int launch_tc(const CUtensorMap& km, const CUtensorMap& vm, const Params& p, cudaStream_t st) {
+static int launch_tc(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const Params& p,
+                     cudaStream_t st) {
   auto kern = attn_tc_kernel<D, kBF16>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::kSmem);
   const int grid = static_cast<int>(std::min<int64_t>(p.items, current_sm_count()));
-  kern<<<grid, kAttnThreads, Cfg<D>::kSmem, st>>>(km, vm, p);
+  kern<<<grid, kAttnThreads, Cfg<D>::kSmem, st>>>(qm, km, vm, p);
   return check_launch("attn_tc_kernel");
 }
 
@@ -769,13 +759,14 @@ extern "C" int cab_sparse_attn_fwd(const void* q, const void* k, const void* v, 
     pair_union_kernel<<<ugrid, 128, usmem, st>>>(up);
     if (int rc = check_launch("pair_union_kernel")) return rc;
 
-    CUtensorMap km{}, vm{};
+    CUtensorMap qm{}, km{}, vm{};
     auto mk = [&](CUtensorMap* m, const void* ptr, int64_t H, const int64_t* s, uint32_t rows) {
       uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(N), static_cast<uint64_t>(H), static_cast<uint64_t>(B)};
       uint64_t str[3] = {static_cast<uint64_t>(s[2]) * es, static_cast<uint64_t>(s[1]) * es, static_cast<uint64_t>(s[0]) * es};
       uint32_t box[4] = {64, rows, 1, 1};
       return make_tensor_map(m, tma_type(dtype), 4, ptr, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
     };
+    if (int rc = mk(&qm, q, Hq, q_strides, 128)) return rc;
     if (int rc = mk(&km, k, Hkv, k_strides, 64)) return rc;
     if (int rc = mk(&vm, v, Hkv, v_strides, 64)) return rc;
     Params p{};
@@ -801,8 +792,8 @@ extern "C" int cab_sparse_attn_fwd(const void* q, const void* k, const void* v, 
     p.scale_log2 = softmax_scale * kLog2e;
     p.causal = causal != 0;
     const bool bf = dtype == CAB_DTYPE_BF16;
-    if (D == 128) return bf ? launch_tc<128, true>(km, vm, p, st) : launch_tc<128, false>(km, vm, p, st);
-    return bf ? launch_tc<64, true>(km, vm, p, st) : launch_tc<64, false>(km, vm, p, st);
+    if (D == 128) return bf ? launch_tc<128, true>(qm, km, vm, p, st) : launch_tc<128, false>(qm, km, vm, p, st);
+    return bf ? launch_tc<64, true>(qm, km, vm, p, st) : launch_tc<64, false>(qm, km, vm, p, st);
   }
 
   if (block_size > 128 || D > 128)
