@@ -51,6 +51,29 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Packed two-wide fp32 arithmetic (one instruction for two lanes of work).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
@@ -464,20 +487,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         // it from there, and S(g + 3) waits for that PV before reusing the buffer.
         float ls[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
         if (all_full) {
-          const float nm = -m_run;
+          // two keys per instruction for the scale-and-shift and the running sums
+          const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+          const float2 nm2 = make_float2(-m_run, -m_run);
+          float2 acc2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             uint32_t w[16];
 #pragma unroll
             for (int y = 0; y < 16; ++y) {
               const int c = 32 * hh + 2 * y;
-              const float p0 = ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, nm));
-              const float p1 = ex2(fmaf(__uint_as_float(s[c + 1]), p.scale_log2, nm));
-              ls[y & 3] += p0 + p1;
+              const float2 x2 = ffma2(make_float2(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), sc2, nm2);
+              const float p0 = ex2(x2.x), p1 = ex2(x2.y);
+              acc2[y & 1] = fadd2(acc2[y & 1], make_float2(p0, p1));
               w[y] = pack2<kBF16>(p0, p1);
             }
             tmem_st16(scol + 16 * hh, w);
           }
+          ls[0] = acc2[0].x;
+          ls[1] = acc2[0].y;
+          ls[2] = acc2[1].x;
+          ls[3] = acc2[1].y;
         } else if (any_live) {
           const bool live = m_run != -INFINITY;
 #pragma unroll
