@@ -146,15 +146,12 @@ class Layer:
         return out, kv_num
 
     def e2e(self, q_host, k_host, v_host, out_host):
-        """Public-API call with host buffers: H2D inputs, layer, D2H output."""
-        dev = torch.device("cuda", torch.cuda.current_device())
-        q = q_host.to(dev, non_blocking=True)
-        k = k_host.to(dev, non_blocking=True)
-        v = v_host.to(dev, non_blocking=True)
-        kv_idx, kv_num = self.pred.predict_blocks(q, k)
-        from cab_attention.kernels import block_sparse_attention
-        out = block_sparse_attention(q, k, v, kv_idx, kv_num, BLOCK, self.cfg["causal"])
-        out_host.copy_(out, non_blocking=True)
+        """Public-API call with host buffers (cab_prefill_host): the pinned inputs are
+        copied in and the output copied back inside the call, streamed per (b, KV head)
+        unit so the copies overlap the compute; returns after the output has landed."""
+        from cab_attention import prefill_from_host
+        prefill_from_host(q_host, k_host, v_host, block_size=BLOCK, sparsity=self.cfg["sparsity"],
+                          lambda_redundancy=LAMBDA, causal=self.cfg["causal"], out=out_host)
 
 
 def cpu_sample(cfg, seconds_budget, seed=0):

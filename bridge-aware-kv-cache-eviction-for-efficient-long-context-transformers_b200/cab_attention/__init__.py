@@ -4,7 +4,8 @@ Public surface (the reference's import paths, ``README.md:77,117``):
 ``from cab_attention import CABAttention``;
 ``from cab_attention.coarse_predictor import CoarseCurvaturePredictor``;
 ``cab_attention.kernels.coarsening``, ``cab_attention.kernels.frc_kernel`` and
-``cab_attention.kernels.sparse_attention`` for the individual stages. Every op runs the
+``cab_attention.kernels.sparse_attention`` for the individual stages;
+``cab_attention.prefill_from_host`` for the whole path over page-locked host tensors. Every op runs the
 sm_100a kernels of ``libcab_b200.so`` through its C ABI (``include/cab_capi.h``).
 """
 
@@ -12,5 +13,6 @@ __version__ = "1.0.0"
 
 from .cab_attention import CABAttention  # noqa: E402
 from .coarse_predictor import CoarseCurvaturePredictor  # noqa: E402
+from .host_prefill import prefill_from_host  # noqa: E402
 
-__all__ = ["CABAttention", "CoarseCurvaturePredictor"]
+__all__ = ["CABAttention", "CoarseCurvaturePredictor", "prefill_from_host"]

@@ -9,6 +9,7 @@
 #include "topk.cu"
 #include "sparse_attn.cu"
 #include "noalloc.cu"
+#include "prefill_host.cu"
 
 extern "C" int cab_get_version(void) { return CAB_API_VERSION; }
 

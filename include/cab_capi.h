@@ -187,6 +187,37 @@ CAB_API int cab_sparse_attn_fwd_noalloc(const void* q, const void* k, const void
                                         const int64_t* v_strides, const int64_t* o_strides,
                                         float softmax_scale, int causal, int dtype, void* stream);
 
+/* Scratch bytes cab_prefill_host needs for these sizes (two device slots of one
+ * (batch, KV head) unit each). `keep` = blocks kept per query-block row. */
+CAB_API int cab_prefill_host_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t N,
+                                            int64_t D, int64_t block_size, int64_t keep,
+                                            int dtype, int normalization, size_t* bytes);
+
+/*
+ * The whole prefill path for inputs and outputs in HOST memory: per (b, query head)
+ * cab_coarsen_maxl2 -> cab_frc -> cab_topk_blocks (k = keep) -> cab_sparse_attn_fwd, with
+ * the same arguments and results as calling those four entry points on device copies of
+ * the tensors (bit-identical outputs).
+ * q/out [B,Hq,N,D] and k/v [B,Hkv,N,D] are dense host tensors; kv_idx [B,Hq,M,keep] and
+ * kv_num [B,Hq,M] (int32, may be NULL) receive the block lists. All host buffers must be
+ * page-locked (cudaHostAlloc / cudaHostRegister); anything else is CAB_ERR_INVALID_ARG.
+ * The work is streamed one (b, KV head) unit at a time through two device slots of the
+ * workspace: the host->device copy of the next unit and the device->host copy of the
+ * previous one (on two library-owned copy streams of the current device) overlap the
+ * compute of this one (on `stream`). Asynchronous like every entry point: it starts after
+ * the work already queued on `stream`, later work on `stream` starts after all of its
+ * copies, and the host buffers must stay valid (and `out` unread) until then.
+ * No counterpart in the reference (an addition of this library): its callers move whole
+ * tensors between host and device around the layer.
+ */
+CAB_API int cab_prefill_host(const void* q, const void* k, const void* v, void* out,
+                             int32_t* kv_idx, int32_t* kv_num, int64_t B, int64_t Hq,
+                             int64_t Hkv, int64_t N, int64_t D, int64_t block_size, int64_t keep,
+                             float temperature, float lambda_redundancy, int normalization,
+                             int formula, int redundancy_scale, int select_high,
+                             int keep_diagonal, int causal, float softmax_scale, int dtype,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -58,6 +58,17 @@ def test_argument_checks_without_gpu(lib):
     # Hq not a multiple of Hkv
     assert lib.cab_frc(fake, fake, fake, None, None, 1, 3, 2, 100, 64, 2, 1.0, 0.5, 0, 0, 0,
                        fake, n.value, None) == 1
+    # host prefill: NULL input, keep outside [1, M], host memory that is not page-locked
+    args = (1, 2, 2, 256, 64, 64)
+    assert lib.cab_prefill_host(None, fake, fake, fake, None, None, *args, 1, 1.0, 0.5, 0, 0, 0,
+                                1, 1, 0, 0.125, 2, fake, 1 << 30, None) == 1
+    assert lib.cab_prefill_host(fake, fake, fake, fake, None, None, *args, 5, 1.0, 0.5, 0, 0, 0,
+                                1, 1, 0, 0.125, 2, fake, 1 << 30, None) == 1
+    buf = ctypes.create_string_buffer(2 * 256 * 64 * 2)
+    hb = ctypes.cast(buf, ctypes.c_void_p)
+    assert lib.cab_prefill_host(hb, hb, hb, hb, None, None, *args, 1, 1.0, 0.5, 0, 0, 0,
+                                1, 1, 0, 0.125, 2, fake, 1 << 30, None) == 1
+    assert b"page-locked" in lib.cab_last_error_string()
 
 
 def test_workspace_queries(lib):
@@ -66,6 +77,13 @@ def test_workspace_queries(lib):
     assert n.value >= 2 * 8 * 1000 * (2 * 100 + 2) * 4
     assert lib.cab_sparse_attn_workspace_size(1, 8, 4096, 64, 64, 6, 0, ctypes.byref(n)) == 0
     assert n.value == 0  # fp32 runs the CUDA-core kernel, which needs no scratch
+    # host prefill: two slots of one (b, KV head) unit, independent of B and Hkv
+    one = _lib._c_size(0)
+    assert lib.cab_prefill_host_workspace_size(1, 8, 8, 128000, 128, 64, 100, 2, 0,
+                                               ctypes.byref(one)) == 0
+    assert lib.cab_prefill_host_workspace_size(2, 8, 8, 128000, 128, 64, 100, 2, 0,
+                                               ctypes.byref(n)) == 0
+    assert n.value == one.value and n.value >= 2 * (4 * 128000 * 128 * 2 + 2000 * 2000 * 4)
 
 
 def test_ops_refuse_cpu_tensors():
