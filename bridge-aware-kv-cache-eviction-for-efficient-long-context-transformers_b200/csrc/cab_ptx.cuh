@@ -84,6 +84,35 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* c
   }
 }
 
+// A monotonically increasing shared-memory counter published with release semantics and
+// read with acquire semantics (CTA scope).
+__device__ __forceinline__ uint32_t counter_load(const uint32_t* c) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(c)) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void counter_store(uint32_t* c, uint32_t v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(c)), "r"(v) : "memory");
+}
+
+// Waits until *c >= target, with the same bound and abort rules as mbar_wait.
+__device__ __forceinline__ bool counter_wait(const uint32_t* c, uint32_t target, int* cta_abort = nullptr) {
+  if (counter_load(c) >= target) return true;
+  uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (counter_load(c) >= target) return true;
+    if ((i & 63u) == 0u) {
+      if (cta_abort && *reinterpret_cast<volatile int*>(cta_abort)) return false;
+      if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        atomicOr(&g_device_status, CAB_DEVICE_TIMEOUT);
+        if (cta_abort) *reinterpret_cast<volatile int*>(cta_abort) = 1;
+        return false;
+      }
+    }
+  }
+}
+
 // Orders this thread's generic-proxy shared-memory accesses before later async-proxy
 // (TMA / tensor core) accesses of the same memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -6,18 +6,18 @@
 //    `pair_union_kernel` into one ascending list whose entries carry two flags (kept by
 //    block 2p / by block 2p+1); key blocks are consumed two at a time (a 128-key tile).
 //    A block kept by only one of the two query blocks is masked for the other 64 rows.
-//  * Warp 0 streams K and V tiles with TMA (128-byte swizzle) into 4/3-stage (D=128) or
-//    6/6-stage (D=64) shared-memory rings. The softmax warps write each item's Q rows
-//    into TMEM. One thread of warp 1 issues S = Q K^T (M=128, N=128, K=D; Q from TMEM, K
-//    from shared memory) into one of two TMEM S buffers and, one tile behind,
-//    O += P V (P from TMEM, V read MN-major from its natural [keys, D] layout; M=128,
-//    N=D, K=128), so S(t+1) overlaps the softmax of t. Only K and V are ever read from
-//    shared memory by the tensor core, which keeps its operand traffic well inside the
-//    shared-memory bandwidth that it also shares with the TMA writes.
+//  * Warp 0 streams each item's Q tile (double-buffered, so the next item's Q lands while
+//    this item finishes) and the K and V tiles with TMA (128-byte swizzle) into
+//    shared-memory rings. One thread of warp 1 issues S = Q K^T (M=128, N=128, K=D; both
+//    operands K-major from shared memory) into one of three TMEM S buffers; one thread of
+//    warp 10 issues O += P V (P from TMEM where the softmax wrote it over its S, V read
+//    MN-major from its natural [keys, D] layout; M=128, N=D, K=128). Three buffers keep
+//    S(g+1), S(g+2) and PV(g-1) in flight while tile g is in the softmax. Warp 11 consumes
+//    the PV completions in order and publishes their count.
 //  * Warps 2-9, two per row (one per 64-key block of the tile): tcgen05.ld of the S row
-//    half, exact masking (flags, causal token mask, sequence end), online softmax in the
-//    exp2 domain with a lazy rescale of O (only when the running max grows by more than
-//    2^8), P stored to TMEM over the S columns it came from, and the final O / l
+//    half, exact masking (union flags, causal token mask, sequence end), online softmax
+//    in the exp2 domain with a lazy rescale of O (only when the running max grows by more
+//    than 2^8), P stored to TMEM over the S columns it came from, and the final O / l
 //    epilogue.
 //  * Items run (b, h, p)-major so the CTAs in flight share one head's K/V in L2.
 //
@@ -151,11 +151,12 @@ struct Cfg {
   static constexpr int kQBytes = 128 * D * 2;
   static constexpr int kKBytes = 128 * D * 2;  // one tile = two 64-key blocks
   static constexpr int kVBytes = 128 * D * 2;
-  static constexpr int kKStages = D == 128 ? 3 : 5;
+  static constexpr int kQStages = 2;  // the next item's Q lands while this item finishes
+  static constexpr int kKStages = D == 128 ? 2 : 5;
   static constexpr int kVStages = D == 128 ? 3 : 5;
-  static constexpr int kTileBytes = kQBytes + kKStages * kKBytes + kVStages * kVBytes;
+  static constexpr int kTileBytes = kQStages * kQBytes + kKStages * kKBytes + kVStages * kVBytes;
   static constexpr int kXchgBytes = 2 * 2 * 128 * 4;  // row-max / row-sum exchange [parity][kb][row]
-  static constexpr int kAuxBytes = kXchgBytes + 512;   // + mbarriers (<= 62), TMEM slot, abort flag
+  static constexpr int kAuxBytes = kXchgBytes + 512;   // + mbarriers (<= 41), TMEM slot, abort flag, counter
   // Tiles start at the first 1024-byte boundary of the dynamic shared memory; the kernel
   // checks at run time that tiles + aux fit in what it was given.
   static constexpr int kSmemWanted = kTileBytes + kAuxBytes + 1024;
@@ -170,11 +171,24 @@ constexpr int kSBufs = 3;
 constexpr uint32_t kTmemO = 384;
 
 // Warp 0: TMA producer; warp 1: issues S = Q K^T; warps 2-9: softmax; warp 10: issues
-// O += P V. Two issuing threads keep the tensor pipe queued: while one blocks on a full
-// MMA queue, the other's group is already waiting behind it.
+// O += P V; warp 11: PV completion tracker. Two issuing threads keep the tensor pipe
+// queued: while one blocks on a full MMA queue, the other's group is already waiting
+// behind it.
+//
+// Barrier discipline. Every mbarrier wait is a parity wait, which is only sound while the
+// barrier is at most one phase past the phase waited for, and an arrival count is only
+// sound while no arrival for a later phase can overtake one for the current phase. Each
+// barrier below is therefore waited phase after phase by one consumer, or made safe by a
+// dependency: P(g) arrives on p_full[g % 3], and a warp can only reach tile g + 3 after
+// PV(g) consumed p_full(g). PV completions (o_ready[g & 1]) are consumed in order by
+// warp 11 alone, which publishes their count in `pv_seen`; the PV issuer starts PV(g)
+// only once PV(g - 2) has been seen, so o_ready never runs two phases ahead of warp 11,
+// while PV(g - 1) and PV(g) can still be queued together. Softmax threads wait on that
+// count only when they must rescale O (rare) and in the epilogue.
 constexpr int kSoftmaxWarps = 8;
 constexpr int kPvWarp = 2 + kSoftmaxWarps;
-constexpr int kAttnThreads = 32 * (kPvWarp + 1);
+constexpr int kTrackWarp = kPvWarp + 1;
+constexpr int kAttnThreads = 32 * (kTrackWarp + 1);
 
 struct Params {
   int32_t B, Hq, Hkv, N, M, P;
@@ -214,7 +228,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = base;
-  uint8_t* sK = sQ + C::kQBytes;
+  uint8_t* sK = sQ + C::kQStages * C::kQBytes;
   uint8_t* sV = sK + C::kKStages * C::kKBytes;
   uint8_t* sEnd = sV + C::kVStages * C::kVBytes;
   float* xchg = reinterpret_cast<float*>(sEnd);
@@ -227,33 +241,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       return;  // shared memory base not aligned as expected: nothing was touched
     }
   }
-  uint64_t* q_full = bar;
-  uint64_t* q_empty = bar + 1;
-  uint64_t* k_full = bar + 2;
+  uint64_t* q_full = bar;                   // [kQStages] by item
+  uint64_t* q_empty = bar + C::kQStages;    // [kQStages]
+  uint64_t* k_full = bar + 2 * C::kQStages;
   uint64_t* k_empty = k_full + C::kKStages;
   uint64_t* v_full = k_empty + C::kKStages;
   uint64_t* v_empty = v_full + C::kVStages;
   uint64_t* s_full = v_empty + C::kVStages;
   uint64_t* buf_free = s_full + kSBufs;  // S/P buffer reusable: PV of its last tile completed
   uint64_t* p_full = buf_free + kSBufs;
-  uint64_t* o_ready = p_full + 1;
-  uint64_t* o_free = o_ready + 1;
+  uint64_t* o_ready = p_full + kSBufs;  // [2]
+  uint64_t* o_free = o_ready + 2;
   uint64_t* drain = o_free + 1;     // [0] S issuer, [1] PV issuer
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  uint32_t* pv_seen = reinterpret_cast<uint32_t*>(abort_flag + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     prefetch_tensormap(&qmap);
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
+    for (int s = 0; s < C::kQStages; ++s) { mbar_init(&q_full[s], 1); mbar_init(&q_empty[s], 1); }
     for (int s = 0; s < C::kKStages; ++s) { mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1); }
     for (int s = 0; s < C::kVStages; ++s) { mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1); }
     for (int s = 0; s < kSBufs; ++s) { mbar_init(&s_full[s], 1); mbar_init(&buf_free[s], 1); }
-    mbar_init(p_full, kSoftmaxWarps);
-    mbar_init(o_ready, 1);
+    for (int s = 0; s < kSBufs; ++s) mbar_init(&p_full[s], kSoftmaxWarps);
+    mbar_init(&o_ready[0], 1);
+    mbar_init(&o_ready[1], 1);
+    *pv_seen = 0u;
     mbar_init(o_free, kSoftmaxWarps);
     mbar_init(&drain[0], 1);
     mbar_init(&drain[1], 1);
@@ -279,10 +295,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int bh = static_cast<int>(item / p.P), pr = static_cast<int>(item % p.P);
         const int b = bh / p.Hq, h = bh % p.Hq, hk = h / G;
         const uint32_t* ul = p.ulist + item * p.stride;
-        if (!mbar_wait(q_empty, (gi & 1) ^ 1, abort_flag)) { ok = false; break; }
-        mbar_arrive_expect_tx(q_full, C::kQBytes);
+        const int qs = static_cast<int>(gi % C::kQStages);
+        if (!mbar_wait(&q_empty[qs], ((gi / C::kQStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(&q_full[qs], C::kQBytes);
 #pragma unroll
-        for (int a = 0; a < C::kAtoms; ++a) tma_load_4d(sQ + a * 16384, &qmap, q_full, 64 * a, 128 * pr, h, b);
+        for (int a = 0; a < C::kAtoms; ++a)
+          tma_load_4d(sQ + qs * C::kQBytes + a * 16384, &qmap, &q_full[qs], 64 * a, 128 * pr, h, b);
         ++gi;
         for (int t = 0; t < T; ++t) {
           const int j0 = static_cast<int>(ul[2 * t] & kIdxMask), j1 = static_cast<int>(ul[2 * t + 1] & kIdxMask);
@@ -327,8 +345,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
         const int T = p.ntiles[item];
         if (T == 0) continue;
-        if (!mbar_wait(q_full, gi & 1, abort_flag)) { ok = false; break; }
+        const int qs = static_cast<int>(gi % C::kQStages);
+        if (!mbar_wait(&q_full[qs], (gi / C::kQStages) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after_sync();
+        const uint64_t dq = dQ + static_cast<uint64_t>((qs * C::kQBytes) >> 4);
         for (int t = 0; t < T; ++t) {
           // S(g) = Q K(g)^T into buffer g % 3 once PV(g - 3) (which read P(g - 3) there)
           // has completed; Q and K from shared memory (K-major)
@@ -342,14 +362,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint64_t off = (kk >> 2) * (16384 >> 4) + (kk & 3) * (32 >> 4);
-            mma_f16_ss(d_s, dQ + off, dk + off, idesc_s, kk > 0 ? 1u : 0u);
+            mma_f16_ss(d_s, dq + off, dk + off, idesc_s, kk > 0 ? 1u : 0u);
           }
           mma_commit(&k_empty[ks]);
           mma_commit(&s_full[buf]);
           ++kt;
         }
         if (!ok) break;
-        mma_commit(q_empty);
+        mma_commit(&q_empty[qs]);
         gt += T;
         ++gi;
       }
@@ -373,9 +393,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           // P from TMEM (in its S buffer), V from shared memory (MN-major)
           const uint32_t g = gt + t;
           const int vs = vt % C::kVStages;
-          if (!mbar_wait(p_full, g & 1, abort_flag) ||
+          if (!mbar_wait(&p_full[g % kSBufs], (g / kSBufs) & 1, abort_flag) ||
               !mbar_wait(&v_full[vs], (vt / C::kVStages) & 1, abort_flag)) { ok = false; break; }
           if (t == 0 && gi > 0 && !mbar_wait(o_free, (gi - 1) & 1, abort_flag)) { ok = false; break; }
+          if (g >= 2 && !counter_wait(pv_seen, g - 1, abort_flag)) { ok = false; break; }
           tc_fence_after_sync();
           const uint64_t dv = dV + static_cast<uint64_t>((vs * C::kVBytes) >> 4);
           const uint32_t pt = tmem + (g % kSBufs) * 128;
@@ -384,7 +405,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             mma_f16_ts(tmem_o, pt + (kk >> 2) * 64 + (kk & 3) * 8,
                        dv + static_cast<uint64_t>(kk * (2048 >> 4)), idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
           mma_commit(&v_empty[vs]);
-          mma_commit(o_ready);
+          mma_commit(&o_ready[g & 1]);
           mma_commit(&buf_free[g % kSBufs]);
           ++vt;
         }
@@ -395,6 +416,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (gi > 0) {
         mma_commit(&drain[1]);
         (void)mbar_wait(&drain[1], 0, nullptr);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kTrackWarp) {
+    if (lane == 0) {
+      uint32_t gt = 0;
+      bool ok = true;
+      for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
+        const int T = p.ntiles[item];
+        for (int t = 0; t < T; ++t) {
+          const uint32_t g = gt + t;
+          if (!mbar_wait(&o_ready[g & 1], (g >> 1) & 1, abort_flag)) { ok = false; break; }
+          counter_store(pv_seen, g + 1);
+        }
+        gt += T;
       }
     }
     __syncwarp();
@@ -414,8 +450,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     constexpr int kHalfD = D / 2;
     using InT = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
     uint32_t gt = 0;
+    // The tile count and this thread's first list entry of each item are loaded one item
+    // ahead, so their global-memory latency is not paid at the item boundary.
+    int T_next = 0;
+    uint32_t e_first_next = 0u;
+    if (static_cast<int64_t>(blockIdx.x) < p.items) {
+      T_next = __ldg(p.ntiles + blockIdx.x);
+      e_first_next = __ldg(p.ulist + static_cast<int64_t>(blockIdx.x) * p.stride + kb);
+    }
     for (int64_t item = blockIdx.x; item < p.items; item += gridDim.x) {
-      const int T = p.ntiles[item];
+      const int T = T_next;
+      const uint32_t e_first = e_first_next;
+      {
+        const int64_t nitem = item + gridDim.x;
+        if (nitem < p.items) {
+          T_next = __ldg(p.ntiles + nitem);
+          e_first_next = __ldg(p.ulist + nitem * p.stride + kb);
+        }
+      }
       const int bh = static_cast<int>(item / p.P), pr = static_cast<int>(item % p.P);
       const int b = bh / p.Hq, h = bh % p.Hq;
       const int row = 128 * pr + r;
@@ -432,7 +484,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint32_t* ul = p.ulist + item * p.stride;
       float m_run = -INFINITY, l = 0.f;
       bool ok = true;
-      uint32_t e_next = ul[kb];
+      uint32_t e_next = e_first;
       for (int t = 0; t < T; ++t) {
         const uint32_t g = gt + t, buf = g % kSBufs;
         const uint32_t e = e_next;
@@ -535,12 +587,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
         // O may only be rescaled once PV(g - 1) has finished accumulating into it. The
         // wait sits at the end of the tile: PV(g - 1) ran while this tile's exps did.
-        if (t > 0) {
-          const bool okp = mbar_wait(o_ready, (g - 1) & 1, abort_flag);
+        if (__any_sync(0xffffffffu, need)) {
+          const bool okp = counter_wait(pv_seen, g, abort_flag);
           if (!__all_sync(0xffffffffu, okp)) { ok = false; break; }
           tc_fence_after_sync();
-        }
-        if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
           for (int c = kb * kHalfD; c < (kb + 1) * kHalfD; c += 16) {
             uint32_t o[16];
@@ -554,12 +604,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         tc_fence_before_sync();
         __syncwarp();
-        if (lane == 0) mbar_arrive(p_full);
+        if (lane == 0) mbar_arrive(&p_full[buf]);
       }
       if (!ok) break;
       // ---- epilogue: O / l, each thread writes its half of the row's D columns
       const uint32_t glast = gt + T - 1;
-      const bool oko = mbar_wait(o_ready, glast & 1, abort_flag);
+      const bool oko = counter_wait(pv_seen, glast + 1, abort_flag);
       if (!__all_sync(0xffffffffu, oko)) break;
       tc_fence_after_sync();
       float* xs = xchg + (T & 1) * 256;
