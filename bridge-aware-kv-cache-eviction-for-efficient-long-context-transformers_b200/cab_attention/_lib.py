@@ -54,6 +54,11 @@ SIGNATURES = {
     "cab_sparse_attn_fwd_noalloc": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64,
                                     _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_ptr,
                                     _c_ptr, _c_ptr, _c_ptr, _c_float, _c_int, _c_int, _c_ptr],
+    "cab_flash_attn_workspace_size": [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_int,
+                                      ctypes.POINTER(_c_size)],
+    "cab_flash_attn_fwd": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64,
+                           _c_i64, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_float, _c_int,
+                           _c_int, _c_ptr, _c_size, _c_ptr],
     "cab_prefill_host_workspace_size": [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                                         _c_int, _c_int, ctypes.POINTER(_c_size)],
     "cab_prefill_host": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64,

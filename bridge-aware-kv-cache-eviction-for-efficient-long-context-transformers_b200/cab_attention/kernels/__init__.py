@@ -4,3 +4,5 @@ from .coarsening import coarsen_max_l2, coarsen_qk_max_l2, coarsen_qk_max_l2_pyt
 from .frc_kernel import (compute_block_frc, generate_block_mask, keep_count,  # noqa: F401
                          topk_blocks, visualize_frc_statistics)
 from .sparse_attention import block_sparse_attention  # noqa: F401
+from .flash_attention_accumulate import (flash_attention_forward,  # noqa: F401
+                                         flash_attention_with_cumulative_scores)

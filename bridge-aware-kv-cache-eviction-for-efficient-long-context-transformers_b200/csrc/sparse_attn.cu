@@ -145,18 +145,22 @@ __global__ void __launch_bounds__(128) pair_union_kernel(const UnionParams p) {
 }
 
 // ------------------------------------------------------------------ tensor-core kernel
-template <int D>
+// kDense: every item is one 128-row query block against all key tiles in order (the
+// flash-attention forward with optional column scores); one Q buffer suffices there (items
+// are long), and the space holds the column-score exchange slots.
+template <int D, bool kDense = false>
 struct Cfg {
   static constexpr int kAtoms = D / 64;
   static constexpr int kQBytes = 128 * D * 2;
   static constexpr int kKBytes = 128 * D * 2;  // one tile = two 64-key blocks
   static constexpr int kVBytes = 128 * D * 2;
-  static constexpr int kQStages = 2;  // the next item's Q lands while this item finishes
+  static constexpr int kQStages = kDense ? 1 : 2;  // sparse: the next item's Q lands while this item finishes
   static constexpr int kKStages = D == 128 ? 2 : 5;
   static constexpr int kVStages = D == 128 ? 3 : 5;
   static constexpr int kTileBytes = kQStages * kQBytes + kKStages * kKBytes + kVStages * kVBytes;
-  static constexpr int kXchgBytes = 2 * 2 * 128 * 4;  // row-max / row-sum exchange [parity][kb][row]
-  static constexpr int kAuxBytes = kXchgBytes + 512;   // + mbarriers (<= 41), TMEM slot, abort flag, counter
+  static constexpr int kSlotBytes = kDense ? 2 * 2 * 4 * 32 * 8 : 0;  // column sums [parity][kb][quad][lane] float2
+  static constexpr int kXchgBytes = 2 * 2 * 128 * 4 + kSlotBytes;  // + row-max / row-sum exchange [parity][kb][row]
+  static constexpr int kAuxBytes = kXchgBytes + 512;   // + mbarriers (<= 54), TMEM slot, abort flag, counter
   // Tiles start at the first 1024-byte boundary of the dynamic shared memory; the kernel
   // checks at run time that tiles + aux fit in what it was given.
   static constexpr int kSmemWanted = kTileBytes + kAuxBytes + 1024;
@@ -175,6 +179,14 @@ constexpr uint32_t kTmemO = 384;
 // queued: while one blocks on a full MMA queue, the other's group is already waiting
 // behind it.
 //
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // Barrier discipline. Every mbarrier wait is a parity wait, which is only sound while the
 // barrier is at most one phase past the phase waited for, and an arrival count is only
 // sound while no arrival for a later phase can overtake one for the current phase. Each
@@ -191,7 +203,8 @@ constexpr int kTrackWarp = kPvWarp + 1;
 constexpr int kAttnThreads = 32 * (kTrackWarp + 1);
 
 struct Params {
-  int32_t B, Hq, Hkv, N, M, P;
+  int32_t B, Hq, Hkv, Nq, Nk, M, P;  // sparse: Nq == Nk == N; dense: P = query blocks of 128 rows
+  int32_t Tk;                        // dense: key tiles (128 keys) per query block
   int64_t items;
   const void* q;
   int64_t q_s0, q_s1, q_s2;
@@ -203,7 +216,31 @@ struct Params {
   int32_t stride;
   float scale_log2;
   int32_t causal;
+  float* colsum;      // dense: [B, Hq, Nk] column scores, accumulated (may be null)
+  int64_t cs_s0, cs_s1;
+  float* partial;     // dense + colsum: per-CTA private column sums [gridDim.x, pstride], zeroed
+  int64_t pstride;
 };
+
+// Tiles of an item: the merged list length (sparse) or the key tiles up to the causal
+// limit (dense).
+template <bool kDense>
+__device__ __forceinline__ int item_tiles(const Params& p, int64_t item) {
+  if constexpr (kDense) {
+    const int pr = static_cast<int>(item % p.P);
+    return p.causal ? min(p.Tk, pr + 1) : p.Tk;
+  } else {
+    return __ldg(p.ntiles + item);
+  }
+}
+
+// List entry of key block kb (0/1) of tile t: block index | kept-by-first-half << 30 |
+// kept-by-second-half << 31.
+template <bool kDense>
+__device__ __forceinline__ uint32_t item_entry(const uint32_t* ul, int t, int kb) {
+  if constexpr (kDense) return static_cast<uint32_t>(2 * t + kb) | 0xC0000000u;
+  else return ul[2 * t + kb];
+}
 
 template <bool kBF16>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
@@ -216,15 +253,12 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   }
 }
 
-__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
 
-template <int D, bool kBF16>
+template <int D, bool kBF16, bool kDense>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, const Params p) {
-  using C = Cfg<D>;
+  using C = Cfg<D, kDense>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = base;
@@ -232,6 +266,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sV = sK + C::kKStages * C::kKBytes;
   uint8_t* sEnd = sV + C::kVStages * C::kVBytes;
   float* xchg = reinterpret_cast<float*>(sEnd);
+  float2* colslots = reinterpret_cast<float2*>(xchg + 512);  // dense: [parity * 2 + kb][quad][lane]
   uint64_t* bar = reinterpret_cast<uint64_t*>(sEnd + C::kXchgBytes);
   {
     uint32_t dyn;
@@ -253,7 +288,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* o_ready = p_full + kSBufs;  // [2]
   uint64_t* o_free = o_ready + 2;
   uint64_t* drain = o_free + 1;     // [0] S issuer, [1] PV issuer
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
+  // The column-sum rendezvous barriers take one arrival per warp: the warp's lanes write
+  // shared memory, __syncwarp() orders those writes before lane 0's (release) arrival.
+  uint64_t* cs_full = drain + 2;    // dense: [parity * 2 + kb] column sums of quads 1-3 posted (3)
+  uint64_t* cs_free = cs_full + 4;  // dense: [parity * 2 + kb] slots read by quad 0 (1)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cs_free + 4);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   uint32_t* pv_seen = reinterpret_cast<uint32_t*>(abort_flag + 1);
 
@@ -273,6 +312,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     mbar_init(o_free, kSoftmaxWarps);
     mbar_init(&drain[0], 1);
     mbar_init(&drain[1], 1);
+    for (int s = 0; s < 4; ++s) {
+      mbar_init(&cs_full[s], 3);
+      mbar_init(&cs_free[s], 1);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -290,7 +333,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       uint32_t gi = 0, kt = 0, vt = 0;
       bool ok = true;
       for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
-        const int T = p.ntiles[item];
+        const int T = item_tiles<kDense>(p, item);
         if (T == 0) continue;
         const int bh = static_cast<int>(item / p.P), pr = static_cast<int>(item % p.P);
         const int b = bh / p.Hq, h = bh % p.Hq, hk = h / G;
@@ -303,7 +346,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tma_load_4d(sQ + qs * C::kQBytes + a * 16384, &qmap, &q_full[qs], 64 * a, 128 * pr, h, b);
         ++gi;
         for (int t = 0; t < T; ++t) {
-          const int j0 = static_cast<int>(ul[2 * t] & kIdxMask), j1 = static_cast<int>(ul[2 * t + 1] & kIdxMask);
+          const int j0 = static_cast<int>(item_entry<kDense>(ul, t, 0) & kIdxMask);
+          const int j1 = static_cast<int>(item_entry<kDense>(ul, t, 1) & kIdxMask);
           const int ks = kt % C::kKStages;
           if (!mbar_wait(&k_empty[ks], ((kt / C::kKStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&k_full[ks], C::kKBytes);
@@ -343,7 +387,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       uint32_t gi = 0, kt = 0, gt = 0;
       bool ok = true;
       for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
-        const int T = p.ntiles[item];
+        const int T = item_tiles<kDense>(p, item);
         if (T == 0) continue;
         const int qs = static_cast<int>(gi % C::kQStages);
         if (!mbar_wait(&q_full[qs], (gi / C::kQStages) & 1, abort_flag)) { ok = false; break; }
@@ -387,7 +431,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       uint32_t gi = 0, vt = 0, gt = 0;
       bool ok = true;
       for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
-        const int T = p.ntiles[item];
+        const int T = item_tiles<kDense>(p, item);
         if (T == 0) continue;
         for (int t = 0; t < T; ++t) {
           // P from TMEM (in its S buffer), V from shared memory (MN-major)
@@ -424,7 +468,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       uint32_t gt = 0;
       bool ok = true;
       for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
-        const int T = p.ntiles[item];
+        const int T = item_tiles<kDense>(p, item);
         for (int t = 0; t < T; ++t) {
           const uint32_t g = gt + t;
           if (!mbar_wait(&o_ready[g & 1], (g >> 1) & 1, abort_flag)) { ok = false; break; }
@@ -445,7 +489,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int kb = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
     const int half = r >> 6;
+    // Row-pair exchanges (tile maxima, final row sums) alternate between two buffers; `xc`
+    // counts this thread's exchanges. A buffer is rewritten two exchanges later, after the
+    // partner has passed the exchange in between, i.e. after it has read the buffer. The
+    // pair meets at named barrier 1 + quad (64 threads). A warp that leaves the loops
+    // early (a bounded wait gave up, which also raised the CTA abort flag) arrives at that
+    // barrier once on its way out, so a partner blocked there is released, sees the flag
+    // and leaves too; the barrier is never waited on without a way out.
     const int pair_bar = 1 + quad;
+    uint32_t xc = 0;
+    bool alive = true;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     constexpr int kHalfD = D / 2;
     using InT = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
@@ -455,17 +508,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     int T_next = 0;
     uint32_t e_first_next = 0u;
     if (static_cast<int64_t>(blockIdx.x) < p.items) {
-      T_next = __ldg(p.ntiles + blockIdx.x);
-      e_first_next = __ldg(p.ulist + static_cast<int64_t>(blockIdx.x) * p.stride + kb);
+      T_next = item_tiles<kDense>(p, blockIdx.x);
+      e_first_next = kDense ? item_entry<kDense>(nullptr, 0, kb) : __ldg(p.ulist + static_cast<int64_t>(blockIdx.x) * p.stride + kb);
     }
+    int dense_tiles_seen = 0;  // dense + column sums: key tiles touched in this CTA's private buffer
     for (int64_t item = blockIdx.x; item < p.items; item += gridDim.x) {
       const int T = T_next;
       const uint32_t e_first = e_first_next;
       {
         const int64_t nitem = item + gridDim.x;
         if (nitem < p.items) {
-          T_next = __ldg(p.ntiles + nitem);
-          e_first_next = __ldg(p.ulist + nitem * p.stride + kb);
+          T_next = item_tiles<kDense>(p, nitem);
+          e_first_next = kDense ? item_entry<kDense>(nullptr, 0, kb) : __ldg(p.ulist + nitem * p.stride + kb);
         }
       }
       const int bh = static_cast<int>(item / p.P), pr = static_cast<int>(item % p.P);
@@ -474,23 +528,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int64_t ooff = b * p.o_s0 + h * p.o_s1 + static_cast<int64_t>(row) * p.o_s2;
       InT* orow = reinterpret_cast<InT*>(p.out) + ooff + kb * kHalfD;
       if (T == 0) {
-        if (row < p.N) {
+        if (row < p.Nq) {
 #pragma unroll
           for (int c = 0; c < kHalfD; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
-          if (p.lse && kb == 0) p.lse[static_cast<int64_t>(bh) * p.N + row] = -INFINITY;
+          if (p.lse && kb == 0) p.lse[static_cast<int64_t>(bh) * p.Nq + row] = -INFINITY;
         }
         continue;
       }
-      const uint32_t* ul = p.ulist + item * p.stride;
+      const uint32_t* ul = kDense ? nullptr : p.ulist + item * p.stride;
       float m_run = -INFINITY, l = 0.f;
+      float m_exact = -INFINITY;  // dense column scores: exact running max (log2 units)
       bool ok = true;
       uint32_t e_next = e_first;
       for (int t = 0; t < T; ++t) {
         const uint32_t g = gt + t, buf = g % kSBufs;
         const uint32_t e = e_next;
-        if (t + 1 < T) e_next = ul[2 * (t + 1) + kb];
+        if (t + 1 < T) e_next = item_entry<kDense>(ul, t + 1, kb);
         const int j = static_cast<int>(e & kIdxMask);
-        int lim = ((e >> (30 + half)) & 1u) ? min(64, p.N - 64 * j) : 0;
+        int lim = ((e >> (30 + half)) & 1u) ? min(64, p.Nk - 64 * j) : 0;
         if (p.causal) lim = min(lim, row - 64 * j + 1);
         lim = max(lim, 0);
         const bool any_live = __any_sync(0xffffffffu, lim > 0);
@@ -521,9 +576,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-        float* xs = xchg + (t & 1) * 256;
+        float* xs = xchg + (xc & 1u) * 256;
         xs[kb * 128 + r] = mx;
         named_bar_sync(pair_bar, 64);
+        ++xc;
+        if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(abort_flag) != 0)) { ok = false; break; }
         const float m_tile = fmaxf(mx, xs[(kb ^ 1) * 128 + r]) * p.scale_log2;  // -inf stays -inf
         float alpha = 1.f;
         bool need = false;
@@ -553,6 +610,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               const float p0 = ex2(x2.x), p1 = ex2(x2.y);
               acc2[y & 1] = fadd2(acc2[y & 1], make_float2(p0, p1));
               w[y] = pack2<kBF16>(p0, p1);
+              if constexpr (kDense) {
+                s[c] = __float_as_uint(p0);
+                s[c + 1] = __float_as_uint(p1);
+              }
             }
             tmem_st16(scol + 16 * hh, w);
           }
@@ -572,6 +633,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               const float p1 = (c + 1 < lim && live) ? ex2(fmaf(__uint_as_float(s[c + 1]), p.scale_log2, -m_run)) : 0.f;
               ls[y & 3] += p0 + p1;
               w[y] = pack2<kBF16>(p0, p1);
+              if constexpr (kDense) {
+                s[c] = __float_as_uint(p0);
+                s[c + 1] = __float_as_uint(p1);
+              }
             }
             tmem_st16(scol + 16 * hh, w);
           }
@@ -581,9 +646,59 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int y = 0; y < 16; ++y) w[y] = 0u;
           tmem_st16(scol, w);
           tmem_st16(scol + 16, w);
+          if constexpr (kDense) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) s[c] = 0u;
+          }
         }
         tmem_wait_st();
         l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        if constexpr (kDense) {
+          if (p.colsum != nullptr) {
+            // Column scores as the reference accumulates them: exp(s - m) summed over the
+            // rows, with m the exact running row max after this tile. P above is relative to
+            // the lazily updated m_run, so each row's terms are scaled by 2^(m_run - m_exact);
+            // rows past the query end add nothing.
+            m_exact = fmaxf(m_exact, m_tile);
+            const float cq = (row < p.Nq && m_exact != -INFINITY) ? ex2(m_run - m_exact) : 0.f;
+            float v[64];
+#pragma unroll
+            for (int c = 0; c < 64; ++c) v[c] = __uint_as_float(s[c]) * cq;
+            // sum over the warp's 32 rows: five halving exchange steps leave lane l with
+            // the sums of columns 2l and 2l + 1
+#pragma unroll
+            for (int stp = 0; stp < 5; ++stp) {
+              const int hw = 32 >> stp, off = 16 >> stp;
+              const bool up = (lane & off) != 0;
+#pragma unroll
+              for (int i = 0; i < hw; ++i) {
+                const float send = up ? v[i] : v[i + hw];
+                const float keep = up ? v[i + hw] : v[i];
+                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+              }
+            }
+            // the four row quadrants of this key block meet in shared memory; quadrant 0
+            // adds their sum to this CTA's private column buffer
+            const int sb = static_cast<int>(g & 1u) * 2 + kb;
+            float2* slot = colslots + sb * 128;
+            if (quad != 0) {
+              const bool okf = mbar_wait(&cs_free[sb], ((g >> 1) & 1u) ^ 1u, abort_flag);
+              if (!__all_sync(0xffffffffu, okf)) { ok = false; break; }
+              slot[quad * 32 + lane] = make_float2(v[0], v[1]);
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&cs_full[sb]);
+            } else {
+              const bool okf = mbar_wait(&cs_full[sb], (g >> 1) & 1u, abort_flag);
+              if (!__all_sync(0xffffffffu, okf)) { ok = false; break; }
+              const float2 a1 = slot[32 + lane], a2 = slot[64 + lane], a3 = slot[96 + lane];
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&cs_free[sb]);
+              float2* pp = reinterpret_cast<float2*>(p.partial + static_cast<int64_t>(blockIdx.x) * p.pstride +
+                                                     128 * t + 64 * kb + 2 * lane);
+              atomicAdd(pp, make_float2((v[0] + a1.x) + (a2.x + a3.x), (v[1] + a1.y) + (a2.y + a3.y)));
+            }
+          }
+        }
 
         // O may only be rescaled once PV(g - 1) has finished accumulating into it. The
         // wait sits at the end of the tile: PV(g - 1) ran while this tile's exps did.
@@ -606,24 +721,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[buf]);
       }
-      if (!ok) break;
+      if (!ok) {
+        alive = false;
+        break;
+      }
       // ---- epilogue: O / l, each thread writes its half of the row's D columns
       const uint32_t glast = gt + T - 1;
       const bool oko = counter_wait(pv_seen, glast + 1, abort_flag);
-      if (!__all_sync(0xffffffffu, oko)) break;
+      if (!__all_sync(0xffffffffu, oko)) {
+        alive = false;
+        break;
+      }
       tc_fence_after_sync();
-      float* xs = xchg + (T & 1) * 256;
+      float* xs = xchg + (xc & 1u) * 256;
       xs[kb * 128 + r] = l;
       named_bar_sync(pair_bar, 64);
+      ++xc;
+      if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(abort_flag) != 0)) { alive = false; break; }
       const float l_row = l + xs[(kb ^ 1) * 128 + r];
-      named_bar_sync(pair_bar, 64);  // both have read before either reuses the buffer
       const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
 #pragma unroll
       for (int c = 0; c < kHalfD; c += 16) {
         uint32_t o[16];
         tmem_ld16(tmem_o + lane_addr + kb * kHalfD + c, o);
         tmem_wait_ld();
-        if (row < p.N) {
+        if (row < p.Nq) {
 #pragma unroll
           for (int x = 0; x < 16; x += 8) {
             uint32_t wv[4];
@@ -634,13 +756,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
       }
-      if (row < p.N && p.lse && kb == 0)
-        p.lse[static_cast<int64_t>(bh) * p.N + row] = l_row > 0.f ? (m_run + __log2f(l_row)) * kLn2 : -INFINITY;
+      if (row < p.Nq && p.lse && kb == 0)
+        p.lse[static_cast<int64_t>(bh) * p.Nq + row] = l_row > 0.f ? (m_run + __log2f(l_row)) * kLn2 : -INFINITY;
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(o_free);
+      if constexpr (kDense) {
+        // Flush this CTA's private column sums into the caller's scores when the next item
+        // belongs to another (b, h) (or there is none), and clear them.
+        if (p.colsum != nullptr && quad == 0) {
+          dense_tiles_seen = max(dense_tiles_seen, T);
+          const int64_t nitem = item + gridDim.x;
+          if (nitem >= p.items || nitem / p.P != item / p.P) {
+            float* part = p.partial + static_cast<int64_t>(blockIdx.x) * p.pstride;
+            float* dst = p.colsum + b * p.cs_s0 + h * p.cs_s1;
+            for (int t2 = 0; t2 < dense_tiles_seen; ++t2) {
+              const int key = 128 * t2 + 64 * kb + 2 * lane;
+              float2* pp = reinterpret_cast<float2*>(part + key);
+              const float2 val = *pp;
+              if (key < p.Nk) atomicAdd(dst + key, val.x);
+              if (key + 1 < p.Nk) atomicAdd(dst + key + 1, val.y);
+              *pp = make_float2(0.f, 0.f);
+            }
+            dense_tiles_seen = 0;
+          }
+        }
+      }
       gt += T;
     }
+    if (!alive) named_bar_arrive(pair_bar, 64);  // release a partner blocked at the pair barrier
   }
   tc_fence_before_sync();
   __syncthreads();
@@ -764,14 +908,41 @@ static bool use_tensor_cores(int dtype, int64_t D, int64_t bs) {
   return (dtype == CAB_DTYPE_BF16 || dtype == CAB_DTYPE_F16) && bs == 64 && (D == 64 || D == 128);
 }
 
-template <int D, bool kBF16>
+template <int D, bool kBF16, bool kDense>
 static int launch_tc(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const Params& p,
-                     cudaStream_t st) {
-  auto kern = attn_tc_kernel<D, kBF16>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::kSmem);
-  const int grid = static_cast<int>(std::min<int64_t>(p.items, current_sm_count()));
-  kern<<<grid, kAttnThreads, Cfg<D>::kSmem, st>>>(qm, km, vm, p);
+                     int grid, cudaStream_t st) {
+  auto kern = attn_tc_kernel<D, kBF16, kDense>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D, kDense>::kSmem);
+  kern<<<grid, kAttnThreads, Cfg<D, kDense>::kSmem, st>>>(qm, km, vm, p);
   return check_launch("attn_tc_kernel");
+}
+
+// Q / K / V / O tensor map over [B, H, rows, D] with {b, h, n} strides in elements.
+static int attn_tensor_map(CUtensorMap* m, const void* ptr, int64_t B, int64_t H, int64_t rows, int64_t D,
+                           const int64_t* s, size_t es, int dtype, uint32_t box_rows) {
+  uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(rows), static_cast<uint64_t>(H),
+                      static_cast<uint64_t>(B)};
+  uint64_t str[3] = {static_cast<uint64_t>(s[2]) * es, static_cast<uint64_t>(s[1]) * es,
+                     static_cast<uint64_t>(s[0]) * es};
+  uint32_t box[4] = {64, box_rows, 1, 1};
+  return make_tensor_map(m, tma_type(dtype), 4, ptr, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// Dense (flash) forward: CTAs in the launch and the private column-buffer stride.
+struct FlashLayout {
+  int grid;
+  int64_t items, Tk, pstride;
+  size_t partial_bytes;
+};
+
+static FlashLayout flash_layout(int64_t B, int64_t Hq, int64_t Nq, int64_t Nk) {
+  FlashLayout L{};
+  L.items = B * Hq * ((Nq + 127) / 128);
+  L.Tk = (Nk + 127) / 128;
+  L.pstride = L.Tk * 128;
+  L.grid = static_cast<int>(std::min<int64_t>(L.items, current_sm_count()));
+  L.partial_bytes = static_cast<size_t>(L.grid) * L.pstride * sizeof(float);
+  return L;
 }
 
 }  // namespace attn
@@ -840,20 +1011,15 @@ extern "C" int cab_sparse_attn_fwd(const void* q, const void* k, const void* v, 
     if (int rc = check_launch("pair_union_kernel")) return rc;
 
     CUtensorMap qm{}, km{}, vm{};
-    auto mk = [&](CUtensorMap* m, const void* ptr, int64_t H, const int64_t* s, uint32_t rows) {
-      uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(N), static_cast<uint64_t>(H), static_cast<uint64_t>(B)};
-      uint64_t str[3] = {static_cast<uint64_t>(s[2]) * es, static_cast<uint64_t>(s[1]) * es, static_cast<uint64_t>(s[0]) * es};
-      uint32_t box[4] = {64, rows, 1, 1};
-      return make_tensor_map(m, tma_type(dtype), 4, ptr, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
-    };
-    if (int rc = mk(&qm, q, Hq, q_strides, 128)) return rc;
-    if (int rc = mk(&km, k, Hkv, k_strides, 64)) return rc;
-    if (int rc = mk(&vm, v, Hkv, v_strides, 64)) return rc;
+    if (int rc = attn_tensor_map(&qm, q, B, Hq, N, D, q_strides, es, dtype, 128)) return rc;
+    if (int rc = attn_tensor_map(&km, k, B, Hkv, N, D, k_strides, es, dtype, 64)) return rc;
+    if (int rc = attn_tensor_map(&vm, v, B, Hkv, N, D, v_strides, es, dtype, 64)) return rc;
     Params p{};
     p.B = static_cast<int32_t>(B);
     p.Hq = static_cast<int32_t>(Hq);
     p.Hkv = static_cast<int32_t>(Hkv);
-    p.N = static_cast<int32_t>(N);
+    p.Nq = static_cast<int32_t>(N);
+    p.Nk = static_cast<int32_t>(N);
     p.M = static_cast<int32_t>(M);
     p.P = up.P;
     p.items = L.items;
@@ -872,8 +1038,10 @@ extern "C" int cab_sparse_attn_fwd(const void* q, const void* k, const void* v, 
     p.scale_log2 = softmax_scale * kLog2e;
     p.causal = causal != 0;
     const bool bf = dtype == CAB_DTYPE_BF16;
-    if (D == 128) return bf ? launch_tc<128, true>(qm, km, vm, p, st) : launch_tc<128, false>(qm, km, vm, p, st);
-    return bf ? launch_tc<64, true>(qm, km, vm, p, st) : launch_tc<64, false>(qm, km, vm, p, st);
+    const int grid = static_cast<int>(std::min<int64_t>(p.items, current_sm_count()));
+    if (D == 128)
+      return bf ? launch_tc<128, true, false>(qm, km, vm, p, grid, st) : launch_tc<128, false, false>(qm, km, vm, p, grid, st);
+    return bf ? launch_tc<64, true, false>(qm, km, vm, p, grid, st) : launch_tc<64, false, false>(qm, km, vm, p, grid, st);
   }
 
   if (block_size > 128 || D > 128)
@@ -905,4 +1073,87 @@ extern "C" int cab_sparse_attn_fwd(const void* q, const void* k, const void* v, 
       break;
   }
   return check_launch("attn_simt_kernel");
+}
+
+extern "C" int cab_flash_attn_workspace_size(int64_t B, int64_t Hq, int64_t Nq, int64_t Nk, int64_t D, int dtype,
+                                             int with_scores, size_t* bytes) {
+  (void)D;
+  (void)dtype;
+  if (!bytes) return fail(CAB_ERR_INVALID_ARG, "flash_workspace_size: NULL output");
+  if (B <= 0 || Hq <= 0 || Nq <= 0 || Nk <= 0) return fail(CAB_ERR_INVALID_ARG, "flash_workspace_size: non-positive size");
+  *bytes = with_scores ? attn::flash_layout(B, Hq, Nq, Nk).partial_bytes : 0;
+  return CAB_OK;
+}
+
+extern "C" int cab_flash_attn_fwd(const void* q, const void* k, const void* v, void* out, float* scores,
+                                  float* lse, int64_t B, int64_t Hq, int64_t Hkv, int64_t Nq, int64_t Nk,
+                                  int64_t D, const int64_t* q_strides, const int64_t* k_strides,
+                                  const int64_t* v_strides, const int64_t* o_strides, float softmax_scale,
+                                  int causal, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace attn;
+  if (!q || !k || !v || !out) return fail(CAB_ERR_INVALID_ARG, "flash: NULL pointer");
+  if (!q_strides || !k_strides || !v_strides || !o_strides) return fail(CAB_ERR_INVALID_ARG, "flash: NULL strides");
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Nq <= 0 || Nk <= 0 || D <= 0)
+    return fail(CAB_ERR_INVALID_ARG, "flash: non-positive size");
+  if (Hq % Hkv != 0) return fail(CAB_ERR_INVALID_ARG, "flash: Hq %% Hkv != 0");
+  if (!(softmax_scale > 0.f)) return fail(CAB_ERR_INVALID_ARG, "flash: softmax_scale must be > 0");
+  if (causal && Nq != Nk) return fail(CAB_ERR_INVALID_ARG, "flash: causal needs Nq == Nk");
+  if (dtype != CAB_DTYPE_BF16 && dtype != CAB_DTYPE_F16)
+    return fail(CAB_ERR_UNSUPPORTED, "flash: dtype %d (bf16 / f16 only)", dtype);
+  if (D != 64 && D != 128) return fail(CAB_ERR_UNSUPPORTED, "flash: D=%lld (64 or 128 only)", (long long)D);
+  if (Nq >= (int64_t)1 << 30 || Nk >= (int64_t)1 << 30 || B * Hq >= (int64_t)1 << 31)
+    return fail(CAB_ERR_UNSUPPORTED, "flash: sizes exceed int32");
+  const size_t es = dtype_size(dtype);
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || (scores && !aligned16(scores)))
+    return fail(CAB_ERR_INVALID_ARG, "flash: pointers must be 16-byte aligned");
+  const int64_t* ss[4] = {q_strides, k_strides, v_strides, o_strides};
+  for (int x = 0; x < 4; ++x)
+    for (int i = 0; i < 3; ++i)
+      if (ss[x][i] <= 0 || (ss[x][i] * static_cast<int64_t>(es)) % 16 != 0)
+        return fail(CAB_ERR_INVALID_ARG, "flash: strides must be positive multiples of 16 bytes");
+  const FlashLayout L = flash_layout(B, Hq, Nq, Nk);
+  if (scores) {
+    if (!workspace || workspace_bytes < L.partial_bytes)
+      return fail(CAB_ERR_WORKSPACE, "flash: workspace of %zu bytes needed, %zu given", L.partial_bytes, workspace_bytes);
+    if (!aligned16(workspace)) return fail(CAB_ERR_INVALID_ARG, "flash: workspace must be 16-byte aligned");
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUtensorMap qm{}, km{}, vm{};
+  if (int rc = attn_tensor_map(&qm, q, B, Hq, Nq, D, q_strides, es, dtype, 128)) return rc;
+  if (int rc = attn_tensor_map(&km, k, B, Hkv, Nk, D, k_strides, es, dtype, 64)) return rc;
+  if (int rc = attn_tensor_map(&vm, v, B, Hkv, Nk, D, v_strides, es, dtype, 64)) return rc;
+  if (scores && cudaMemsetAsync(workspace, 0, L.partial_bytes, st) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(CAB_ERR_LAUNCH, "flash: clearing the workspace failed");
+  }
+  Params p{};
+  p.B = static_cast<int32_t>(B);
+  p.Hq = static_cast<int32_t>(Hq);
+  p.Hkv = static_cast<int32_t>(Hkv);
+  p.Nq = static_cast<int32_t>(Nq);
+  p.Nk = static_cast<int32_t>(Nk);
+  p.M = static_cast<int32_t>((Nk + 63) / 64);
+  p.P = static_cast<int32_t>((Nq + 127) / 128);
+  p.Tk = static_cast<int32_t>(L.Tk);
+  p.items = L.items;
+  p.q = q;
+  p.q_s0 = q_strides[0];
+  p.q_s1 = q_strides[1];
+  p.q_s2 = q_strides[2];
+  p.o_s0 = o_strides[0];
+  p.o_s1 = o_strides[1];
+  p.o_s2 = o_strides[2];
+  p.out = out;
+  p.lse = lse;
+  p.scale_log2 = softmax_scale * kLog2e;
+  p.causal = causal != 0;
+  p.colsum = scores;
+  p.cs_s0 = Hq * Nk;
+  p.cs_s1 = Nk;
+  p.partial = scores ? static_cast<float*>(workspace) : nullptr;
+  p.pstride = L.pstride;
+  const bool bf = dtype == CAB_DTYPE_BF16;
+  if (D == 128)
+    return bf ? launch_tc<128, true, true>(qm, km, vm, p, L.grid, st) : launch_tc<128, false, true>(qm, km, vm, p, L.grid, st);
+  return bf ? launch_tc<64, true, true>(qm, km, vm, p, L.grid, st) : launch_tc<64, false, true>(qm, km, vm, p, L.grid, st);
 }

@@ -1,15 +1,16 @@
 // K3: per-row top-k block selection (HBM-bound on reading the score matrix).
 //
 // One warp owns one row (b, h, i) of the [BH, M, M] score matrix at a time. It reads the
-// row once (coalesced, 16-byte loads when M % 4 == 0) and stores it in shared memory as
-// order-preserving 32-bit keys: the preferred direction (select_high or not) maps to
-// "larger key", NaN to the least preferred real key, -0 to +0, excluded (causal j > i)
-// candidates to 0 and the forced diagonal to 0xFFFFFFFF. An MSB-first radix select over
-// the ordinary keys (8-bit digits, 256-bin shared-memory histogram) starts at the highest
-// bit in which the row's keys differ and stops as soon as the boundary bin is taken
-// whole, which gives the threshold tau. A final pass in index order takes every key >
-// tau and the lowest-index keys == tau until k_i are taken, compacting with ballots so
-// kv_idx comes out ascending, and writes the dense 0/1 mask of the row.
+// row once (coalesced, 16-byte loads when M % 4 == 0, eight per lane in flight) and stores
+// it in shared memory as order-preserving 32-bit keys: the preferred direction
+// (select_high or not) maps to "larger key", NaN to the least preferred real key, -0 to
+// +0, excluded (causal j > i) candidates to 0 and the forced diagonal to 0xFFFFFFFF. An
+// MSB-first radix select over the ordinary keys (8-bit digits, 256-bin shared-memory
+// histogram) starts at the highest bit in which the row's keys differ and stops as soon
+// as the boundary bin is taken whole, which gives the threshold tau. A final pass in index order (128 keys per step, four
+// consecutive keys per lane) takes every key > tau and the lowest-index keys == tau until
+// k_i are taken, compacting with warp prefix sums so kv_idx comes out ascending, and
+// writes the dense 0/1 mask of the row.
 //
 // Selection rule: per-(b,h,row) top-k of the Forman-Ricci score (generate_block_mask,
 // called with select_high / keep_diagonal / causal at experiments/longbench_qa/
@@ -42,15 +43,35 @@ __device__ __forceinline__ uint32_t to_key(float f, bool high) {
   return (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
 }
 
+// Exclusive warp prefix sum of v (and the warp total in *total).
+__device__ __forceinline__ uint32_t warp_excl_scan(uint32_t v, int lane, uint32_t* total) {
+  uint32_t incl = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t o = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += o;
+  }
+  *total = __shfl_sync(0xffffffffu, incl, 31);
+  return incl - v;
+}
+
+__device__ __forceinline__ uint32_t key_at(const Params& p, float f, int j, int i, int ncand, bool high) {
+  uint32_t key = to_key(f, high);
+  if (j >= ncand) key = 0u;
+  if (p.keep_diagonal && j == i) key = 0xFFFFFFFFu;
+  return key;
+}
+
 __global__ void __launch_bounds__(256) topk_kernel(const Params p) {
   extern __shared__ __align__(16) uint32_t smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int M = p.M;
   const int row_words = (M + 3) & ~3;
+  const int M4 = row_words >> 2;  // 4-key groups (the tail group is padded with excluded keys)
   uint32_t* keys = smem + static_cast<size_t>(warp) * (row_words + 256);
+  uint4* keys4 = reinterpret_cast<uint4*>(keys);
   uint32_t* hist = keys + row_words;
-  const uint32_t lt_mask = (1u << lane) - 1u;
   const bool high = p.select_high != 0;
 
   for (int64_t row = static_cast<int64_t>(blockIdx.x) * p.warps + warp; row < p.rows;
@@ -60,43 +81,56 @@ __global__ void __launch_bounds__(256) topk_kernel(const Params p) {
     const int kk = min(p.k, ncand);
     const float* src = p.scores + row * M;
 
-    // ---- load the row as keys
+    // ---- load the row as keys (eight loads in flight per lane), tracking the range of
+    // the ordinary keys (neither excluded nor forced)
+    uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
     if ((M & 3) == 0) {
       const float4* src4 = reinterpret_cast<const float4*>(src);
-      for (int j4 = lane; j4 < (M >> 2); j4 += 32) {
-        const float4 v = __ldg(src4 + j4);
-        const float vals[4] = {v.x, v.y, v.z, v.w};
-        uint4 kv;
-        uint32_t* kp = &kv.x;
+      for (int base = lane; base < M4; base += 32 * 8) {
+        float4 v[8];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int j = 4 * j4 + t;
-          uint32_t key = to_key(vals[t], high);
-          if (j >= ncand) key = 0u;
-          if (p.keep_diagonal && j == i) key = 0xFFFFFFFFu;
-          kp[t] = key;
+        for (int u = 0; u < 8; ++u)
+          if (base + 32 * u < M4) v[u] = __ldg(src4 + base + 32 * u);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int j4 = base + 32 * u;
+          if (j4 < M4) {
+            uint4 kv;
+            kv.x = key_at(p, v[u].x, 4 * j4 + 0, i, ncand, high);
+            kv.y = key_at(p, v[u].y, 4 * j4 + 1, i, ncand, high);
+            kv.z = key_at(p, v[u].z, 4 * j4 + 2, i, ncand, high);
+            kv.w = key_at(p, v[u].w, 4 * j4 + 3, i, ncand, high);
+            const uint32_t ks[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+              if (ks[t] != 0u && ks[t] != 0xFFFFFFFFu) {
+                kmin = min(kmin, ks[t]);
+                kmax = max(kmax, ks[t]);
+              }
+            keys4[j4] = kv;
+          }
         }
-        reinterpret_cast<uint4*>(keys)[j4] = kv;
       }
     } else {
-      for (int j = lane; j < M; j += 32) {
-        uint32_t key = to_key(__ldg(src + j), high);
-        if (j >= ncand) key = 0u;
-        if (p.keep_diagonal && j == i) key = 0xFFFFFFFFu;
-        keys[j] = key;
-      }
-    }
-    __syncwarp();
-
-    // ---- radix select among the ordinary keys (the forced diagonal is always taken,
-    // excluded candidates never are). Passes start at the highest bit in which the
-    // row's ordinary keys differ, so bits every key shares cost nothing.
-    uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
-    for (int j = lane; j < M; j += 32) {
-      const uint32_t key = keys[j];
-      if (key != 0u && key != 0xFFFFFFFFu) {
-        kmin = min(kmin, key);
-        kmax = max(kmax, key);
+      for (int base = lane; base < row_words; base += 32 * 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int j = base + 32 * u;
+          v[u] = j < M ? __ldg(src + j) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int j = base + 32 * u;
+          if (j < row_words) {
+            const uint32_t key = j < M ? key_at(p, v[u], j, i, ncand, high) : 0u;
+            if (key != 0u && key != 0xFFFFFFFFu) {
+              kmin = min(kmin, key);
+              kmax = max(kmax, key);
+            }
+            keys[j] = key;
+          }
+        }
       }
     }
 #pragma unroll
@@ -104,6 +138,11 @@ __global__ void __launch_bounds__(256) topk_kernel(const Params p) {
       kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, off));
       kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, off));
     }
+    __syncwarp();
+
+    // ---- radix select among the ordinary keys (the forced diagonal is always taken,
+    // excluded candidates never are). Passes start at the highest bit in which the
+    // row's ordinary keys differ, so bits every key shares cost nothing.
     const int forced = (p.keep_diagonal && i < ncand) ? 1 : 0;
     int remaining = kk - forced;
     // Selection rule applied below: take key > tau, and among keys == tau the lowest
@@ -127,10 +166,13 @@ __global__ void __launch_bounds__(256) topk_kernel(const Params p) {
           const uint32_t dmask = (1u << width) - 1u;
           for (int b = lane; b < 256; b += 32) hist[b] = 0u;
           __syncwarp();
-          for (int j = lane; j < M; j += 32) {
-            const uint32_t key = keys[j];
-            if (key != 0u && key != 0xFFFFFFFFu && (key & pmask) == prefix)
-              atomicAdd(&hist[(key >> lo) & dmask], 1u);
+          for (int j4 = lane; j4 < M4; j4 += 32) {
+            const uint4 kv = keys4[j4];
+            const uint32_t ks[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+              if (ks[t] != 0u && ks[t] != 0xFFFFFFFFu && (ks[t] & pmask) == prefix)
+                atomicAdd(&hist[(ks[t] >> lo) & dmask], 1u);
           }
           __syncwarp();
           // lane l owns bins 255-8l .. 248-8l (highest first)
@@ -141,13 +183,8 @@ __global__ void __launch_bounds__(256) topk_kernel(const Params p) {
             c[t] = hist[255 - 8 * lane - t];
             tot += c[t];
           }
-          uint32_t incl = tot;
-#pragma unroll
-          for (int off = 1; off < 32; off <<= 1) {
-            const uint32_t o = __shfl_up_sync(0xffffffffu, incl, off);
-            if (lane >= off) incl += o;
-          }
-          uint32_t running = incl - tot;
+          uint32_t all;
+          uint32_t running = warp_excl_scan(tot, lane, &all);
           int found_digit = -1;
           uint32_t found_above = 0, found_count = 0;
 #pragma unroll
@@ -186,23 +223,52 @@ __global__ void __launch_bounds__(256) topk_kernel(const Params p) {
         }
       }
     }
-    // ---- select in index order, compact, write outputs
+    // ---- select in index order, 128 keys per step (4 consecutive keys per lane),
+    // compact with warp scans, write outputs
     int32_t* out_idx = p.kv_idx + row * p.k;
     uint8_t* out_dense = p.dense ? p.dense + row * M : nullptr;
-    int eq_seen = 0, taken = 0;
-    for (int base = 0; base < M; base += 32) {
-      const int j = base + lane;
-      const uint32_t key = j < M ? keys[j] : 0u;
-      const bool gt = j < M && key > tau;
-      const bool eq = j < M && key == tau;
-      const uint32_t eq_bits = __ballot_sync(0xffffffffu, eq);
-      const int eq_rank = eq_seen + __popc(eq_bits & lt_mask);
-      const bool take = gt || (eq && eq_rank < take_eq);
-      eq_seen += __popc(eq_bits);
-      const uint32_t take_bits = __ballot_sync(0xffffffffu, take);
-      if (take) out_idx[taken + __popc(take_bits & lt_mask)] = j;
-      taken += __popc(take_bits);
-      if (out_dense && j < M) out_dense[j] = take ? 1 : 0;
+    uint32_t eq_seen = 0, taken = 0;
+    for (int base = 0; base < M4; base += 32) {
+      const int j4 = base + lane;
+      const uint4 kv = j4 < M4 ? keys4[j4] : make_uint4(0u, 0u, 0u, 0u);
+      const uint32_t ks[4] = {kv.x, kv.y, kv.z, kv.w};
+      uint32_t take_bits = 0;
+      if (take_eq == 0) {  // warp-uniform: no ties at tau to split by index
+#pragma unroll
+        for (int t = 0; t < 4; ++t) take_bits |= (ks[t] > tau ? 1u : 0u) << t;
+      } else {
+        uint32_t n_eq = 0;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) n_eq += (ks[t] == tau) ? 1u : 0u;
+        uint32_t eq_total;
+        uint32_t eq_rank = eq_seen + warp_excl_scan(n_eq, lane, &eq_total);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          bool take = ks[t] > tau;
+          if (ks[t] == tau) {
+            take = eq_rank < static_cast<uint32_t>(take_eq);
+            ++eq_rank;
+          }
+          take_bits |= (take ? 1u : 0u) << t;
+        }
+        eq_seen += eq_total;
+      }
+      uint32_t take_total;
+      uint32_t pos = taken + warp_excl_scan(__popc(take_bits), lane, &take_total);
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        if ((take_bits >> t) & 1u) out_idx[pos++] = 4 * j4 + t;
+      taken += take_total;
+      if (out_dense && j4 < M4) {
+        if ((M & 3) == 0) {
+          reinterpret_cast<uchar4*>(out_dense)[j4] =
+              make_uchar4(take_bits & 1u, (take_bits >> 1) & 1u, (take_bits >> 2) & 1u, (take_bits >> 3) & 1u);
+        } else {
+#pragma unroll
+          for (int t = 0; t < 4; ++t)
+            if (4 * j4 + t < M) out_dense[4 * j4 + t] = (take_bits >> t) & 1u;
+        }
+      }
     }
     for (int pos = kk + lane; pos < p.k; pos += 32) out_idx[pos] = -1;
     if (lane == 0) p.kv_num[row] = kk;

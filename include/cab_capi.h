@@ -187,6 +187,35 @@ CAB_API int cab_sparse_attn_fwd_noalloc(const void* q, const void* k, const void
                                         const int64_t* v_strides, const int64_t* o_strides,
                                         float softmax_scale, int causal, int dtype, void* stream);
 
+/* Scratch bytes cab_flash_attn_fwd needs (0 when with_scores is 0). Depends on the
+ * current device's SM count. */
+CAB_API int cab_flash_attn_workspace_size(int64_t B, int64_t Hq, int64_t Nq, int64_t Nk, int64_t D,
+                                          int dtype, int with_scores, size_t* bytes);
+
+/*
+ * Dense attention forward with cumulative column scores:
+ *   out = softmax(q k^T * softmax_scale) v          (each q head h reads KV head h / (Hq/Hkv))
+ *   scores[b,h,j] += sum over queries i of exp(s_ij - m_i(j))
+ * with s_ij = q_i . k_j * softmax_scale and m_i(j) the running row maximum over the keys
+ * of the 128-key blocks 0 .. j/128 (the blocks are visited in order, as the reference's
+ * flash kernel accumulates them; the scores are not normalised by the row sums).
+ * q/out [B,Hq,Nq,D], k/v [B,Hkv,Nk,D] with {b,h,n} strides (elements, 16-byte aligned);
+ * scores [B,Hq,Nk] fp32 dense, accumulated into (may be NULL: no scores, no workspace);
+ * lse [B,Hq,Nq] fp32 natural-log sum-exp (may be NULL). Nq may differ from Nk (a decode
+ * step against a KV cache); causal (an addition: the reference is non-causal) needs
+ * Nq == Nk. bf16/f16 with D in {64, 128}, on tcgen05.
+ * Replaces flash_attention_with_cumulative_scores (cab_attention/kernels/
+ * flash_attention_accumulate.py:169-261, kernel :23-166; callers
+ * experiments/longbench_qa/runner.py:291, experiments/generation_benchmark/driver.py:144
+ * through replace_attention_with_flash).
+ */
+CAB_API int cab_flash_attn_fwd(const void* q, const void* k, const void* v, void* out, float* scores,
+                               float* lse, int64_t B, int64_t Hq, int64_t Hkv, int64_t Nq, int64_t Nk,
+                               int64_t D, const int64_t* q_strides, const int64_t* k_strides,
+                               const int64_t* v_strides, const int64_t* o_strides, float softmax_scale,
+                               int causal, int dtype, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
 /* Scratch bytes cab_prefill_host needs for these sizes (two device slots of one
  * (batch, KV head) unit each). `keep` = blocks kept per query-block row. */
 CAB_API int cab_prefill_host_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t N,

@@ -106,3 +106,26 @@ def test_coarsen_tie_and_partial_block():
     xc, idx = orc.coarsen_maxl2(x, 4)
     assert idx.tolist() == [[[1, 4, 9]]]
     assert (xc[0, 0, 2] == x[0, 0, 9]).all()
+
+
+def test_flash_cumulative_matches_reference_kernel(golden_dir):
+    """The flash restatement against the reference Triton kernel's own outputs
+    (tests/golden/make_flash_golden.py): output to the fp16/bf16 P.V rounding the kernel
+    applies, cumulative column scores to 1e-4 of the largest score."""
+    import torch
+
+    g = np.load(golden_dir / "flash_cumulative.npz")
+    for name in g["names"]:
+        dtype = {"float16": torch.float16, "bfloat16": torch.bfloat16}[str(g[f"{name}/dtype"])]
+        q, k, v = (g[f"{name}/{x}"] for x in "qkv")
+        init = g[f"{name}/init"]
+        start = None
+        if init.shape[2]:
+            start = np.zeros(g[f"{name}/cum"].shape)
+            start[:, :, : init.shape[2]] = init
+        out, cum = orc.flash_attention_cumulative(
+            q, k, v, scores=start, p_round=lambda p: torch.from_numpy(p).to(dtype).double().numpy())
+        tol = 5e-3 if dtype == torch.float16 else 2e-2
+        assert np.abs(out - g[f"{name}/out"]).max() <= tol, name
+        ref = g[f"{name}/cum"].astype(np.float64)
+        assert np.abs(cum - ref).max() <= 1e-4 * max(1.0, np.abs(ref).max()), name
