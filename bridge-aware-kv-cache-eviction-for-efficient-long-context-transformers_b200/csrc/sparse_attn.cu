@@ -653,9 +653,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         tmem_wait_st();
         l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        // O may only be rescaled once PV(g - 1) has finished accumulating into it. The
+        // wait sits at the end of the tile: PV(g - 1) ran while this tile's exps did.
+        if (__any_sync(0xffffffffu, need)) {
+          const bool okp = counter_wait(pv_seen, g, abort_flag);
+          if (!__all_sync(0xffffffffu, okp)) { ok = false; break; }
+          tc_fence_after_sync();
+#pragma unroll
+          for (int c = kb * kHalfD; c < (kb + 1) * kHalfD; c += 16) {
+            uint32_t o[16];
+            tmem_ld16(tmem_o + lane_addr + c, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int x = 0; x < 16; ++x) o[x] = __float_as_uint(__uint_as_float(o[x]) * alpha);
+            tmem_st16(tmem_o + lane_addr + c, o);
+          }
+          tmem_wait_st();
+        }
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[buf]);
         if constexpr (kDense) {
           if (p.colsum != nullptr) {
-            // Column scores as the reference accumulates them: exp(s - m) summed over the
+            // Column scores as the reference accumulates them (after P is released, so the PV
+            // and the next S MMAs do not wait for this work): exp(s - m) summed over the
             // rows, with m the exact running row max after this tile. P above is relative to
             // the lazily updated m_run, so each row's terms are scaled by 2^(m_run - m_exact);
             // rows past the query end add nothing.
@@ -700,26 +721,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
 
-        // O may only be rescaled once PV(g - 1) has finished accumulating into it. The
-        // wait sits at the end of the tile: PV(g - 1) ran while this tile's exps did.
-        if (__any_sync(0xffffffffu, need)) {
-          const bool okp = counter_wait(pv_seen, g, abort_flag);
-          if (!__all_sync(0xffffffffu, okp)) { ok = false; break; }
-          tc_fence_after_sync();
-#pragma unroll
-          for (int c = kb * kHalfD; c < (kb + 1) * kHalfD; c += 16) {
-            uint32_t o[16];
-            tmem_ld16(tmem_o + lane_addr + c, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int x = 0; x < 16; ++x) o[x] = __float_as_uint(__uint_as_float(o[x]) * alpha);
-            tmem_st16(tmem_o + lane_addr + c, o);
-          }
-          tmem_wait_st();
-        }
-        tc_fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[buf]);
       }
       if (!ok) {
         alive = false;
