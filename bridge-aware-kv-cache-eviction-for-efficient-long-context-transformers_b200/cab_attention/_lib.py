@@ -46,6 +46,9 @@ SIGNATURES = {
                 _c_int, _c_float, _c_float, _c_int, _c_int, _c_int, _c_ptr, _c_size, _c_ptr],
     "cab_topk_blocks": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_int, _c_int,
                         _c_int, _c_ptr],
+    "cab_topk_blocks_hybrid": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64,
+                               ctypes.c_double, _c_int, _c_int, _c_int, _c_ptr],
+    "cab_block_maxpool": [_c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_int, _c_ptr],
     "cab_sparse_attn_workspace_size": [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_int,
                                        ctypes.POINTER(_c_size)],
     "cab_sparse_attn_fwd": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64,

@@ -76,10 +76,12 @@ def compute_block_frc(q_coarse: torch.Tensor, k_coarse: torch.Tensor, temperatur
 
 
 def topk_blocks(scores: torch.Tensor, k: int, select_high: bool = True, keep_diagonal: bool = True,
-                causal: bool = False, return_dense: bool = True):
+                causal: bool = False, return_dense: bool = True,
+                magnitude_scores: torch.Tensor | None = None, magnitude_ratio: float = 0.5):
     """Per-row top-k -> ``(kv_idx [B,H,M,k] int32 ascending, -1 padded; kv_num [B,H,M] int32;
-    dense bool [B,H,M,M] or None)``."""
-    _lib.require_cuda(scores)
+    dense bool [B,H,M,M] or None)``. With ``magnitude_scores`` (same shape) the budget is
+    split as in ``generate_block_mask``'s hybrid mode."""
+    _lib.require_cuda(scores, magnitude_scores)
     if scores.dtype != torch.float32:
         scores = scores.float()
     scores = scores.contiguous()
@@ -93,11 +95,23 @@ def topk_blocks(scores: torch.Tensor, k: int, select_high: bool = True, keep_dia
     kv_idx = torch.empty(B, H, M, k, dtype=torch.int32, device=dev)
     kv_num = torch.empty(B, H, M, dtype=torch.int32, device=dev)
     dense = torch.empty(B, H, M, M, dtype=torch.bool, device=dev) if return_dense else None
-    rc = _lib.lib().cab_topk_blocks(scores.data_ptr(), kv_idx.data_ptr(), kv_num.data_ptr(),
-                                    _lib.ptr(dense), B * H, M, k, int(bool(select_high)),
-                                    int(bool(keep_diagonal)), int(bool(causal)),
-                                    _lib.stream_of(scores))
-    _lib.check(rc, "cab_topk_blocks")
+    L = _lib.lib()
+    if magnitude_scores is None:
+        rc = L.cab_topk_blocks(scores.data_ptr(), kv_idx.data_ptr(), kv_num.data_ptr(), _lib.ptr(dense),
+                               B * H, M, k, int(bool(select_high)), int(bool(keep_diagonal)),
+                               int(bool(causal)), _lib.stream_of(scores))
+        _lib.check(rc, "cab_topk_blocks")
+    else:
+        if tuple(magnitude_scores.shape) != (B, H, M, M):
+            raise ValueError("magnitude_scores must have the shape of the FRC scores")
+        if not 0.0 <= float(magnitude_ratio) <= 1.0:
+            raise ValueError("magnitude_ratio must be in [0, 1]")
+        mag = magnitude_scores.float().contiguous()
+        rc = L.cab_topk_blocks_hybrid(scores.data_ptr(), mag.data_ptr(), kv_idx.data_ptr(),
+                                      kv_num.data_ptr(), _lib.ptr(dense), B * H, M, k,
+                                      float(magnitude_ratio), int(bool(select_high)),
+                                      int(bool(keep_diagonal)), int(bool(causal)), _lib.stream_of(scores))
+        _lib.check(rc, "cab_topk_blocks_hybrid")
     return kv_idx, kv_num, dense
 
 
@@ -106,17 +120,39 @@ def generate_block_mask(frc_scores: torch.Tensor, sparsity: float = 0.95, select
                         magnitude_scores: torch.Tensor | None = None, magnitude_ratio: float = 0.5,
                         return_indices: bool = False):
     """Dense bool block mask ``[B,H,M,M]`` (True = keep); with ``return_indices`` also
-    ``(kv_idx, kv_num)`` for ``block_sparse_attention``."""
-    if magnitude_scores is not None:
-        raise NotImplementedError(
-            "the hybrid magnitude/FRC budget split (CAB V4, methods.py:405-553) is not built "
-            "yet; pass magnitude_scores=None")
+    ``(kv_idx, kv_num)`` for ``block_sparse_attention``.
+
+    Hybrid (CAB V4, ``magnitude_scores`` given): per row, after the forced diagonal,
+    ``int(r * magnitude_ratio)`` of the remaining budget ``r`` go to the largest magnitude
+    scores and the rest to the best FRC scores among the blocks not yet taken
+    (``experiments/longbench_qa/methods.py:407-418``: "reserve X% of budget for
+    top-magnitude blocks, (1-X)% for top-FRC blocks")."""
     M = frc_scores.shape[-1]
     kv_idx, kv_num, dense = topk_blocks(frc_scores, keep_count(M, sparsity), select_high,
-                                        keep_diagonal, causal, return_dense=True)
+                                        keep_diagonal, causal, return_dense=True,
+                                        magnitude_scores=magnitude_scores,
+                                        magnitude_ratio=magnitude_ratio)
     if return_indices:
         return dense, kv_idx, kv_num
     return dense
+
+
+def block_max_pool(attention_weights: torch.Tensor, block_size: int = 64) -> torch.Tensor:
+    """Block-level magnitude scores of a dense attention matrix ``[B,H,N,N]``: the maximum
+    of each ``block_size`` x ``block_size`` tile (zero padding of a partial block included),
+    ``[B,H,M,M]`` in the input dtype (``CABV4Attention._coarsen_attention``,
+    ``experiments/longbench_qa/methods.py:535-553``)."""
+    _lib.require_cuda(attention_weights)
+    B, H, N, N2 = attention_weights.shape
+    if N != N2:
+        raise ValueError("attention_weights must be [B, H, N, N]")
+    a = attention_weights.contiguous()
+    M = (N + block_size - 1) // block_size
+    out = torch.empty(B, H, M, M, dtype=torch.float32, device=a.device)
+    rc = _lib.lib().cab_block_maxpool(a.data_ptr(), out.data_ptr(), B * H, N, block_size,
+                                      _lib.dtype_code(a), _lib.stream_of(a))
+    _lib.check(rc, "cab_block_maxpool")
+    return out.to(attention_weights.dtype)
 
 
 def visualize_frc_statistics(frc_scores, affinity=None, triangles=None, save_path=None):

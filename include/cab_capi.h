@@ -138,6 +138,33 @@ CAB_API int cab_topk_blocks(const float* scores, int32_t* kv_idx, int32_t* kv_nu
                     int64_t BH, int64_t M, int64_t k, int select_high, int keep_diagonal,
                     int causal, void* stream);
 
+/*
+ * Hybrid (CAB V4) block selection: cab_topk_blocks with a second score matrix. Per row,
+ * after the forced diagonal, floor(r * magnitude_ratio) of the remaining budget r = k_i - 1
+ * (k_i with keep_diagonal off) go to the candidates with the largest `magnitude` score
+ * ([BH,M,M] fp32, larger preferred, NaN least); the rest go to the best `scores` (direction
+ * select_high) among the candidates not yet taken. Ties go to the lower block index; the
+ * causal rule applies to both parts. Outputs as cab_topk_blocks (the union, ascending).
+ * The reference's generate_block_mask(magnitude_scores=, magnitude_ratio=) is called by
+ * experiments/longbench_qa/methods.py:465-473 and benchmarks/kernel_benchmark.py:201-205
+ * but its implementation is absent from the snapshot; this split is the documented rule of
+ * methods.py:407-418 ("reserve X% of budget for top-magnitude blocks").
+ */
+CAB_API int cab_topk_blocks_hybrid(const float* scores, const float* magnitude, int32_t* kv_idx,
+                                   int32_t* kv_num, uint8_t* dense_mask, int64_t BH, int64_t M,
+                                   int64_t k, double magnitude_ratio, int select_high,
+                                   int keep_diagonal, int causal, void* stream);
+
+/*
+ * Block max-pool of a dense attention matrix: out[bh,I,J] = max over the
+ * block_size x block_size tile (I,J) of attn[bh] ([BH,N,N] dense, f32/f16/bf16), with the
+ * zero padding of a partial last block included (fp32 out [BH,M,M], M = ceil(N/block_size)).
+ * block_size: a power of two in [8, 1024].
+ * Replaces CABV4Attention._coarsen_attention (experiments/longbench_qa/methods.py:535-553).
+ */
+CAB_API int cab_block_maxpool(const void* attn, float* out, int64_t BH, int64_t N, int64_t block_size,
+                              int dtype, void* stream);
+
 /* Scratch bytes cab_sparse_attn_fwd needs for these sizes. */
 CAB_API int cab_sparse_attn_workspace_size(int64_t B, int64_t Hq, int64_t N, int64_t D,
                                    int64_t block_size, int64_t kmax, int dtype, size_t* bytes);

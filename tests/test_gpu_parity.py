@@ -260,3 +260,52 @@ def test_cab_attention_layer_small():
         ctx_t = torch.from_numpy(ctx).float().transpose(1, 2).reshape(2, 2048, 256)
         want = ctx_t.to(torch.bfloat16).cuda() @ layer.proj.weight.t()
         assert (out.float() - want.float()).abs().max().item() <= 2e-2
+
+
+# ------------------------------------------------------------------ hybrid (CAB V4) mask
+@pytest.mark.parametrize("M,k,ratio", [(7, 3, 0.5), (64, 6, 0.25), (130, 13, 0.5), (333, 33, 1.0),
+                                       (512, 25, 0.0), (2000, 100, 0.5), (257, 257, 0.3)])
+@pytest.mark.parametrize("high,diag,causal", [(True, True, False), (False, False, False),
+                                              (True, True, True), (True, False, True)])
+def test_hybrid_topk_bit_exact(M, k, ratio, high, diag, causal):
+    g = np.random.default_rng(M * 7 + k)
+    scores = g.standard_normal((1, 2, M, M)).astype(np.float32)
+    mag = g.random((1, 2, M, M)).astype(np.float32)
+    # ties, NaN and signed zeros in both score matrices
+    scores[0, 0, :, ::5] = scores[0, 0, :, :1]
+    mag[0, 1, :, ::3] = 0.5
+    scores[0, 1, 1, :4] = np.nan
+    mag[0, 0, 2, :3] = np.nan
+    scores[0, 1, 3, :6] = -0.0
+    idx, num, dense = topk_blocks(torch.from_numpy(scores).cuda(), k, high, diag, causal,
+                                  magnitude_scores=torch.from_numpy(mag).cuda(), magnitude_ratio=ratio)
+    widx, wnum, wdense = orc.hybrid_block_mask(scores, mag, k, ratio, high, diag, causal)
+    assert np.array_equal(num.cpu().numpy(), wnum)
+    assert np.array_equal(idx.cpu().numpy(), widx)
+    assert np.array_equal(dense.cpu().numpy(), wdense)
+
+
+def test_generate_block_mask_hybrid_api():
+    from cab_attention.kernels import generate_block_mask
+    g = torch.Generator().manual_seed(3)
+    frc = torch.randn(2, 4, 128, 128, generator=g)
+    mag = torch.rand(2, 4, 128, 128, generator=g)
+    dense, idx, num = generate_block_mask(frc.cuda(), sparsity=0.9, magnitude_scores=mag.cuda(),
+                                          magnitude_ratio=0.5, return_indices=True)
+    k = orc.keep_count(128, 0.9)
+    widx, wnum, wdense = orc.hybrid_block_mask(frc.numpy(), mag.numpy(), k, 0.5)
+    assert np.array_equal(dense.cpu().numpy(), wdense)
+    assert np.array_equal(idx.cpu().numpy(), widx)
+
+
+@pytest.mark.parametrize("dt,N,bs", [("f32", 256, 64), ("bf16", 300, 64), ("f16", 1000, 32),
+                                     ("f32", 77, 8), ("bf16", 2048, 128)])
+def test_block_max_pool_exact(dt, N, bs):
+    from cab_attention.kernels import block_max_pool
+    g = torch.Generator().manual_seed(N)
+    attn = torch.softmax(torch.randn(1, 3, N, N, generator=g), dim=-1).to(DT[dt])
+    attn[0, 1, :5, :7] = -1.0  # negative entries: a padded tile also sees its zero padding
+    got = block_max_pool(attn.cuda(), bs)
+    assert got.dtype == attn.dtype
+    want = orc.block_max_pool(attn.float().numpy(), bs)
+    assert np.array_equal(got.float().cpu().numpy(), want.astype(np.float32))

@@ -129,3 +129,19 @@ def test_flash_cumulative_matches_reference_kernel(golden_dir):
         assert np.abs(out - g[f"{name}/out"]).max() <= tol, name
         ref = g[f"{name}/cum"].astype(np.float64)
         assert np.abs(cum - ref).max() <= 1e-4 * max(1.0, np.abs(ref).max()), name
+
+
+def test_hybrid_limits_reduce_to_plain_topk():
+    """ratio 0 selects by FRC only, ratio 1 by magnitude only (diagonal still forced)."""
+    g = np.random.default_rng(11)
+    f = g.standard_normal((1, 1, 50, 50)).astype(np.float32)
+    m = g.standard_normal((1, 1, 50, 50)).astype(np.float32)
+    for causal in (False, True):
+        i0, n0, d0 = orc.hybrid_block_mask(f, m, 7, 0.0, True, True, causal)
+        j0, _, _ = orc.topk_block_mask(f, 7, True, True, causal)
+        assert np.array_equal(i0, j0)
+        i1, n1, d1 = orc.hybrid_block_mask(f, m, 7, 1.0, True, True, causal)
+        j1, _, _ = orc.topk_block_mask(m, 7, True, True, causal)
+        assert np.array_equal(i1, j1)
+        i5, n5, d5 = orc.hybrid_block_mask(f, m, 7, 0.5, True, True, causal)
+        assert (d5.sum(-1) == n5).all() and all(d5[0, 0, i, i] for i in range(50))
