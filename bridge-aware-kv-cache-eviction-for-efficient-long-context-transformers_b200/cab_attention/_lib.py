@@ -62,6 +62,10 @@ SIGNATURES = {
     "cab_flash_attn_fwd": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64,
                            _c_i64, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_float, _c_int,
                            _c_int, _c_ptr, _c_size, _c_ptr],
+    "cab_node_frc": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_int, _c_ptr],
+    "cab_evict_workspace_size": [_c_i64, _c_i64, _c_int, ctypes.POINTER(_c_size)],
+    "cab_evict_select": [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_i64, _c_i64, ctypes.c_double,
+                         ctypes.c_double, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr],
     "cab_prefill_host_workspace_size": [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                                         _c_int, _c_int, ctypes.POINTER(_c_size)],
     "cab_prefill_host": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64,

@@ -10,6 +10,8 @@
 #include "sparse_attn.cu"
 #include "noalloc.cu"
 #include "prefill_host.cu"
+#include "node_frc.cu"
+#include "evict.cu"
 
 extern "C" int cab_get_version(void) { return CAB_API_VERSION; }
 

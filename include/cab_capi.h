@@ -243,6 +243,38 @@ CAB_API int cab_flash_attn_fwd(const void* q, const void* k, const void* v, void
                                int causal, int dtype, void* workspace, size_t workspace_bytes,
                                void* stream);
 
+/*
+ * Node-level Forman-Ricci curvature of attention graphs attention [batch,N,N] (dense,
+ * f32/f16/bf16): strengths S_i = sum_j A_ij, triangles T_i = sum_j sum_k A_ij A_jk
+ * (= sum_j A_ij S_j), frc F_i = 4 S_i - 2 S_i + 3 T_i; outputs fp32 [batch,N]
+ * (strengths required, triangles may be NULL).
+ * Replaces compute_frc_triton / compute_frc_pytorch / compute_frc
+ * (cab_attention/kernels/frc_triton.py:167-313, exported by cab_attention/kernels/__init__.py:5).
+ */
+CAB_API int cab_node_frc(const void* attention, float* frc, float* strengths, float* triangles,
+                         int64_t batch, int64_t N, int dtype, void* stream);
+
+/* Scratch bytes cab_evict_select needs. */
+CAB_API int cab_evict_workspace_size(int64_t batch, int64_t L, int with_attention, size_t* bytes);
+
+/*
+ * Three-component KV-cache eviction selection, one independent selection per sequence:
+ * budgets local = int(K*local_ratio), bridge = int(K*bridge_ratio), importance = K - both
+ * (each clipped to L); keep [L-local, L), then the `importance` largest scores among the
+ * rest (importance [batch,imp_len] fp32, zero-padded / truncated to L; NULL: the range just
+ * before the local window), then the bridges: with attention [batch,L,L] fp32 and at least
+ * one important position the largest from*to connectivity with the important set, else the
+ * smallest |score - lower median of the unselected scores|, else the positions from one
+ * third into the unselected ones. Ties go to the lower position. Outputs: keep_indices
+ * [batch,K] int64 ascending (-1 padded), counts [batch,4] = kept, local, importance, bridge.
+ * L <= 524288. No host synchronisation.
+ * Replaces ThreeComponentEvictionPolicy.select_indices (cab_attention/eviction/policy.py:40-210).
+ */
+CAB_API int cab_evict_select(const float* importance, int64_t imp_len, const float* attention,
+                             int64_t batch, int64_t L, int64_t keep_size, double local_ratio,
+                             double bridge_ratio, int64_t* keep_indices, int32_t* counts,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
 /* Scratch bytes cab_prefill_host needs for these sizes (two device slots of one
  * (batch, KV head) unit each). `keep` = blocks kept per query-block row. */
 CAB_API int cab_prefill_host_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t N,

@@ -145,3 +145,25 @@ def test_hybrid_limits_reduce_to_plain_topk():
         assert np.array_equal(i1, j1)
         i5, n5, d5 = orc.hybrid_block_mask(f, m, 7, 0.5, True, True, causal)
         assert (d5.sum(-1) == n5).all() and all(d5[0, 0, i, i] for i in range(50))
+
+
+def test_node_frc_matches_reference(golden_dir):
+    """Node-level FRC restatement against the reference's compute_frc_pytorch outputs."""
+    g = np.load(golden_dir / "node_frc.npz")
+    for name in g["names"]:
+        frc, _, _ = orc.node_frc(g[f"{name}/attention"])
+        ref = g[f"{name}/frc"].astype(np.float64)
+        assert np.abs(frc - ref).max() <= 1e-5 * max(1.0, np.abs(ref).max()), name
+
+
+def test_evict_select_matches_reference(golden_dir):
+    """The eviction restatement against the reference's select_indices outputs."""
+    g = np.load(golden_dir / "evict_select.npz")
+    for name in g["names"]:
+        L, K, lr, br = g[f"{name}/params"]
+        imp = g[f"{name}/importance"]
+        att = g[f"{name}/attention"]
+        keep, counts = orc.evict_select(int(L), int(K), imp if imp.size else None, att if att.size else None,
+                                        lr, br)
+        assert np.array_equal(keep, g[f"{name}/keep"]), name
+        assert tuple(counts) == tuple(int(x) for x in g[f"{name}/counts"]), name
