@@ -48,6 +48,13 @@ CONFIGS = {
     "c5": dict(B=1, Hq=32, Hkv=8, N=65536, D=128, sparsity=0.99, causal=True,
                workload="configs[4]: GQA 32/8 B1 N65536 D128 bf16 causal, s=0.99"),
     # the reference's live flash kernel with cumulative column scores (next-row scope)
+    # node-level FRC of attention graphs and the eviction selection (next-row scope)
+    "nodefrc": dict(B=16, Hq=1, Hkv=1, N=4096, D=0, sparsity=0.0, causal=False,
+                    workload="node-level FRC: 16 row-stochastic fp32 attention graphs of 4096 nodes "
+                             "(compute_frc)"),
+    "evict": dict(B=32, Hq=1, Hkv=1, N=131072, D=8192, sparsity=0.0, causal=False,
+                  workload="eviction selection: 32 caches of 131072 tokens, keep 8192 "
+                           "(local 0.3 / bridge 0.2 / importance 0.5, median bridges; select_indices)"),
     "flash": dict(B=1, Hq=8, Hkv=8, N=32768, D=128, sparsity=0.0, causal=False,
                   workload="flash attention + cumulative column scores: B1 H8 N32768 D128 bf16, "
                            "non-causal (flash_attention_with_cumulative_scores)"),
@@ -536,6 +543,108 @@ def run_flash_reference(args, cfg):
     return base
 
 
+# --------------------------------------------------------------------------- nodefrc / evict rows
+def _aux_inputs(cfg, seed):
+    g = torch.Generator().manual_seed(seed)
+    if cfg is CONFIGS["nodefrc"] or cfg.get("D") == 0:
+        a = torch.rand(cfg["B"], cfg["N"], cfg["N"], generator=g)
+        return a / a.sum(dim=-1, keepdim=True)
+    return torch.rand(cfg["B"], cfg["N"], generator=g)
+
+
+def _time_device(fn, steps, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_aux_ours(args, cfg, rank, world, local_rank):
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    hbm, _, _, peak_kind = measured_peaks()
+    x_h = _aux_inputs(cfg, args.seed + rank).pin_memory()
+    x = x_h.to(dev)
+    sampler = ClockSampler(local_rank)
+    if args.config == "nodefrc":
+        from cab_attention.kernels.frc_triton import compute_frc
+        fn = lambda: compute_frc(x)  # noqa: E731
+        metric = "node FRC ms (16 x 4096-node graphs)"
+        nbytes = x.numel() * x.element_size()  # A crosses HBM once (second pass from L2)
+        d2h = cfg["B"] * cfg["N"] * 4
+        e2e_fn = lambda: compute_frc(x_h.to(dev, non_blocking=True)).cpu()  # noqa: E731
+        launches = 2 * cfg["B"]
+    else:
+        from cab_attention.eviction import select_indices_batched
+        K = cfg["D"]
+        fn = lambda: select_indices_batched(cfg["N"], K, x, None, 0.3, 0.2)  # noqa: E731
+        metric = "eviction selection ms (32 caches x 131072 tokens, keep 8192)"
+        nbytes = x.numel() * 4
+        d2h = cfg["B"] * (K * 8 + 16)
+
+        def e2e_fn():
+            keep, counts = select_indices_batched(cfg["N"], K, x_h.to(dev, non_blocking=True), None, 0.3, 0.2)
+            return keep.cpu(), counts.cpu()
+        launches = 2
+    sampler.start()
+    time.sleep(0.3)
+    ms = _time_device(fn, args.steps, args.warmup)
+    clocks = sampler.stop()
+    e2e = _time_device(e2e_fn, args.steps, 1)
+    achieved = nbytes / ms / 1e6
+    return {
+        "metric": metric, "value": ms, "unit": "ms", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded torch.rand)", "config": {"workload": cfg["workload"]},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_source": f"{peak_kind} hbm_gbs", "traffic": None},
+        "cpu_baseline": None,
+        "e2e": {"value": e2e, "unit": "ms", "h2d_bytes_per_step": x.numel() * x.element_size(),
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches * args.steps, "clocks": clocks,
+    }
+
+
+def run_aux_reference(args, cfg):
+    """The reference's own implementation (baseline/_ref) on this GPU: compute_frc (its
+    default Triton path is O(N^3); compute_frc_pytorch, torch.matmul, is timed) and
+    ThreeComponentEvictionPolicy.select_indices once per cache."""
+    import importlib.util
+    name = "kernels/frc_triton.py" if args.config == "nodefrc" else "eviction/policy.py"
+    path = REPO / "baseline" / "_ref" / "cab_attention" / name
+    base = {"metric": "node FRC ms (16 x 4096-node graphs)" if args.config == "nodefrc"
+            else "eviction selection ms (32 caches x 131072 tokens, keep 8192)",
+            "impl": "reference", "unit": "ms", "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "data": "synthetic (seeded torch.rand)", "config": {"workload": cfg["workload"]}}
+    if not path.exists() or not torch.cuda.is_available():
+        base["unavailable"] = "reference module or GPU missing"
+        return base
+    spec = importlib.util.spec_from_file_location("ref_aux", path)
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    x = _aux_inputs(cfg, args.seed).cuda()
+    if args.config == "nodefrc":
+        fn = lambda: [ref.compute_frc_pytorch(x[b]) for b in range(x.shape[0])]  # noqa: E731
+        kernel = "compute_frc_pytorch (torch.matmul) per graph on this GPU"
+    else:
+        pol = ref.ThreeComponentEvictionPolicy(ref.EvictionConfig(0.3, 0.2, 0.5))
+        fn = lambda: [pol.select_indices(cfg["N"], cfg["D"], x[b], None, device="cuda")  # noqa: E731
+                      for b in range(x.shape[0])]
+        kernel = "ThreeComponentEvictionPolicy.select_indices per cache on this GPU"
+    ms = _time_device(fn, args.steps, args.warmup)
+    base.update({"value": ms, "n_gpus": 1, "ms_per_step": ms, "dtype": "f32", "kernel": kernel,
+                 "cpu_baseline": None,
+                 "e2e": {"value": ms, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+    return base
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -565,7 +674,12 @@ def main():
     if args.impl == "reference":
         if rank == 0:
             torch.set_num_threads(os.cpu_count())
-            res = run_flash_reference(args, cfg) if args.config == "flash" else run_reference(args, cfg)
+            if args.config == "flash":
+                res = run_flash_reference(args, cfg)
+            elif args.config in ("nodefrc", "evict"):
+                res = run_aux_reference(args, cfg)
+            else:
+                res = run_reference(args, cfg)
             print(json.dumps(res), flush=True)
         return
 
@@ -574,7 +688,7 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run = run_flash_ours if args.config == "flash" else run_ours
+        run = {"flash": run_flash_ours, "nodefrc": run_aux_ours, "evict": run_aux_ours}.get(args.config, run_ours)
         res = run(args, cfg, rank, world, local_rank)
         if rank == 0 and res is not None:
             print(json.dumps(res), flush=True)

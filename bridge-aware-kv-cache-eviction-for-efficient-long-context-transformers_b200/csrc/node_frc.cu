@@ -8,7 +8,8 @@
 // frc_triton.py:68-118) or as (A @ A).sum(1) (:243-259); both equal A @ S, two
 // matrix-vector passes here. Pass 1: one warp per row, 16-byte loads, fp32 partial sums per
 // lane and a warp reduction. Pass 2: the same row walk against S (read through L1: every
-// warp of a batch reads the same vector) and the fused F epilogue.
+// warp of a batch reads the same vector) and the fused F epilogue. Chunks of matrices that
+// fit in L2 go through both passes before the next chunk, so A crosses HBM once.
 
 #include "cab_host.h"
 
@@ -79,17 +80,28 @@ __global__ void __launch_bounds__(256) frc_kernel(const T* A, const float* S, fl
   }
 }
 
+// The matrices are processed in chunks of at most kL2Chunk bytes, both passes per chunk,
+// so the second pass over a chunk reads it from L2 (126 MB) instead of HBM.
+constexpr int64_t kL2Chunk = 48ll << 20;
+
 template <typename T>
 static int launch(const void* attn, float* F, float* S, float* Tri, int64_t batch, int64_t N, cudaStream_t st) {
   const T* A = static_cast<const T*>(attn);
-  const int64_t rows = batch * N;
   const bool vec = aligned16(attn) && (N * static_cast<int64_t>(sizeof(T))) % 16 == 0;
-  const int64_t warps_needed = rows;
-  const int grid = static_cast<int>(std::min<int64_t>((warps_needed + 7) / 8, (int64_t)current_sm_count() * 8));
-  strengths_kernel<T><<<grid, 256, 0, st>>>(A, S, rows, N, vec);
-  if (int rc = check_launch("node_frc strengths_kernel")) return rc;
-  frc_kernel<T><<<grid, 256, 0, st>>>(A, S, F, Tri, rows, N, vec);
-  return check_launch("node_frc frc_kernel");
+  const int64_t mat_bytes = N * N * static_cast<int64_t>(sizeof(T));
+  const int64_t per_chunk = std::max<int64_t>(1, kL2Chunk / std::max<int64_t>(1, mat_bytes));
+  for (int64_t b0 = 0; b0 < batch; b0 += per_chunk) {
+    const int64_t nb = std::min(per_chunk, batch - b0);
+    const int64_t rows = nb * N;
+    const int grid = static_cast<int>(std::min<int64_t>((rows + 7) / 8, (int64_t)current_sm_count() * 8));
+    const T* Ab = A + b0 * N * N;
+    float* Sb = S + b0 * N;
+    strengths_kernel<T><<<grid, 256, 0, st>>>(Ab, Sb, rows, N, vec);
+    if (int rc = check_launch("node_frc strengths_kernel")) return rc;
+    frc_kernel<T><<<grid, 256, 0, st>>>(Ab, Sb, F + b0 * N, Tri ? Tri + b0 * N : nullptr, rows, N, vec);
+    if (int rc = check_launch("node_frc frc_kernel")) return rc;
+  }
+  return CAB_OK;
 }
 
 }  // namespace nodefrc
