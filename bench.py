@@ -334,9 +334,9 @@ def run_ours(args, cfg, rank, world, local_rank):
 # dram__bytes_read.sum + dram__bytes_write.sum per attention launch from the committed ncu
 # capture (profiles/attn_tc_kernel_ns_4heads.md); None until a capture exists for the
 # workload. "ns": the capture ran the north_star shape at 4 of its 16 (batch, head) units
-# (408.139 MB read + 116.818 MB written); DRAM traffic is per-unit (each unit reads its own
+# (408.579 MB read + 114.571 MB written); DRAM traffic is per-unit (each unit reads its own
 # Q/K/V once and writes its own O), so the full launch is scaled by 16 / 4.
-ATTN_TRAFFIC_BYTES = {"ns": (408.139264e6 + 116.817920e6) * 4}
+ATTN_TRAFFIC_BYTES = {"ns": (408.579072e6 + 114.571264e6) * 4}
 
 
 # --------------------------------------------------------------------------- reference arm
