@@ -276,9 +276,10 @@ def run_ours(args, cfg, rank, world, local_rank):
     B, Hq, Hkv, N, D = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["N"], cfg["D"]
     M = (N + BLOCK - 1) // BLOCK
     kk = layer.pred.keep_per_row(N)
-    coarsen_bytes = (B * Hq + B * Hkv) * (N * D * 2 + M * D * 2)
-    frc_flop = 2.0 * B * Hq * M * M * D + 2.0 * B * Hq * M ** 3
-    topk_bytes = B * Hq * M * M * 4 + B * Hq * M * (kk + 1) * 4
+    from cab_attention import roofline as rl
+    coarsen_bytes = rl.coarsen_bytes(B, Hq, Hkv, N, D, 2, BLOCK)
+    frc_flop = rl.frc_flops(B, Hq, M, D)
+    topk_bytes = rl.topk_bytes(B, Hq, M, kk)
     attn_flop = sparse_attention_flops(kv_num, BLOCK, D)
     c_ms, f_ms, k_ms, a_ms = (float(x) for x in stage_ms)
     stages = {
@@ -376,7 +377,8 @@ def run_reference(args, cfg):
 
 # --------------------------------------------------------------------------- flash row
 def flash_flop(cfg):
-    return 4.0 * cfg["B"] * cfg["Hq"] * cfg["N"] * cfg["N"] * cfg["D"]
+    from cab_attention import roofline as rl
+    return rl.flash_attention_flops(cfg["B"], cfg["Hq"], cfg["N"], cfg["N"], cfg["D"])
 
 
 def run_flash_ours(args, cfg, rank, world, local_rank):

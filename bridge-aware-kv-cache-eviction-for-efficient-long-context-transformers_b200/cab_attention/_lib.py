@@ -38,6 +38,7 @@ SIGNATURES = {
     "cab_last_error_string": [],
     "cab_device_supported": [_c_int],
     "cab_device_status": [_c_ptr, ctypes.POINTER(_c_int)],
+    "cab_selftest_wait_timeout": [_c_i64, _c_ptr, _c_ptr],
     "cab_coarsen_maxl2": [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64,
                           _c_i64, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_int, _c_ptr],
     "cab_frc_workspace_size": [_c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_int,

@@ -62,7 +62,8 @@ class CABAttention(nn.Module):
 
     def forward(self, x: torch.Tensor, return_diagnostics: bool = False):
         B, N, dim = x.shape
-        qkv = self.qkv(x)
+        with torch.cuda.nvtx.range("cab/qkv_proj"):
+            qkv = self.qkv(x)
         q, k, v = self.split_heads(qkv)
         if return_diagnostics:
             dense, diag = self.predictor(q, k, return_diagnostics=True)
@@ -71,9 +72,11 @@ class CABAttention(nn.Module):
             kv_idx, kv_num = self.predictor.predict_blocks(q, k)
         ctx = torch.empty(B, N, dim, dtype=x.dtype, device=x.device)
         ctx_heads = ctx.view(B, N, self.num_heads, self.head_dim).transpose(1, 2)
-        block_sparse_attention(q, k, v, kv_idx, kv_num, self.block_size, causal=self.causal,
-                               out=ctx_heads)
-        out = self.proj(ctx)
+        with torch.cuda.nvtx.range("cab/sparse_attention"):
+            block_sparse_attention(q, k, v, kv_idx, kv_num, self.block_size, causal=self.causal,
+                                   out=ctx_heads)
+        with torch.cuda.nvtx.range("cab/out_proj"):
+            out = self.proj(ctx)
         if return_diagnostics:
             return out, diag
         return out

@@ -8,7 +8,8 @@ and ``benchmarks/benchmark_predictor.py:59-63,114``:
     block_mask, diag = predictor(q, k, return_diagnostics=True)
     predictor.estimate_flops(N, D)                     # {M, coarsening, matmul, triangles, total}
 
-The pipeline is coarsen (K1) -> FRC (K2) -> per-row top-k (K3), all on sm_100a.
+The pipeline is coarsen (K1) -> FRC (K2) -> per-row top-k (K3), all on sm_100a; each
+stage is an NVTX range (``cab/coarsen``, ``cab/frc``, ``cab/topk``) for profilers.
 ``predict_blocks`` returns the index lists the sparse-attention kernel consumes without
 materialising the dense mask or the diagnostics matrices. ``use_triton`` is accepted for
 signature compatibility and ignored (there is one implementation).
@@ -50,25 +51,29 @@ class CoarseCurvaturePredictor(nn.Module):
         return keep_count(self.num_blocks(seq_len), self.sparsity)
 
     def _scores(self, q, k, diagnostics: bool):
-        qc, kc = coarsen_qk_max_l2(q, k, self.block_size)
-        return compute_block_frc(qc, kc, self.temperature, self.lambda_redundancy, self.formula,
-                                 self.normalization, self.redundancy_scale,
-                                 return_affinity=diagnostics, return_redundancy=diagnostics)
+        with torch.cuda.nvtx.range("cab/coarsen"):
+            qc, kc = coarsen_qk_max_l2(q, k, self.block_size)
+        with torch.cuda.nvtx.range("cab/frc"):
+            return compute_block_frc(qc, kc, self.temperature, self.lambda_redundancy, self.formula,
+                                     self.normalization, self.redundancy_scale,
+                                     return_affinity=diagnostics, return_redundancy=diagnostics)
 
     @torch.no_grad()
     def predict_blocks(self, q: torch.Tensor, k: torch.Tensor, return_dense: bool = False):
         """``(kv_idx [B,Hq,M,k] int32, kv_num [B,Hq,M] int32[, dense bool])``."""
         frc, _, _ = self._scores(q, k, diagnostics=False)
-        kv_idx, kv_num, dense = topk_blocks(frc, self.keep_per_row(q.shape[2]), self.select_high,
-                                            self.keep_diagonal, self.causal,
-                                            return_dense=return_dense)
+        with torch.cuda.nvtx.range("cab/topk"):
+            kv_idx, kv_num, dense = topk_blocks(frc, self.keep_per_row(q.shape[2]), self.select_high,
+                                                self.keep_diagonal, self.causal,
+                                                return_dense=return_dense)
         return (kv_idx, kv_num, dense) if return_dense else (kv_idx, kv_num)
 
     @torch.no_grad()
     def forward(self, q: torch.Tensor, k: torch.Tensor, return_diagnostics: bool = False):
         frc, aff, red = self._scores(q, k, diagnostics=return_diagnostics)
-        kv_idx, kv_num, dense = topk_blocks(frc, self.keep_per_row(q.shape[2]), self.select_high,
-                                            self.keep_diagonal, self.causal, return_dense=True)
+        with torch.cuda.nvtx.range("cab/topk"):
+            kv_idx, kv_num, dense = topk_blocks(frc, self.keep_per_row(q.shape[2]), self.select_high,
+                                                self.keep_diagonal, self.causal, return_dense=True)
         if not return_diagnostics:
             return dense
         diag = {

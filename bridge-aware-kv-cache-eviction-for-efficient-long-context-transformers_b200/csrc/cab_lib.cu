@@ -27,6 +27,39 @@ extern "C" int cab_device_supported(int device) {
   return (major == 10 && minor == 0) ? 1 : 0;
 }
 
+namespace cab {
+// Failure-detection self-test: one thread waits on an mbarrier that nothing arrives at,
+// with the bounded-wait pattern of every kernel in this library but a caller-chosen limit;
+// when the limit runs out it records CAB_DEVICE_TIMEOUT and returns. Nothing faults, traps
+// or hangs, and the context stays usable.
+__global__ void wait_timeout_selftest_kernel(uint64_t limit_ns, int* gave_up) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(&bar, 0)) {  // never completes: nothing arrives
+      *gave_up = 0;
+      return;
+    }
+    if ((i & 255u) == 0u && globaltimer_ns() - t0 > limit_ns) {
+      atomicOr(&g_device_status, CAB_DEVICE_TIMEOUT);
+      *gave_up = 1;
+      return;
+    }
+  }
+}
+}  // namespace cab
+
+extern "C" int cab_selftest_wait_timeout(int64_t limit_us, int* gave_up_device, void* stream) {
+  if (!gave_up_device) return cab::fail(CAB_ERR_INVALID_ARG, "selftest: NULL output");
+  if (limit_us <= 0 || limit_us > 10000000) return cab::fail(CAB_ERR_INVALID_ARG, "selftest: limit outside (0, 10 s]");
+  cab::wait_timeout_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint64_t>(limit_us) * 1000ull, gave_up_device);
+  return cab::check_launch("wait_timeout_selftest_kernel");
+}
+
 extern "C" int cab_device_status(void* stream, int* status) {
   if (!status) return cab::fail(CAB_ERR_INVALID_ARG, "device_status: NULL output");
   cudaStream_t st = static_cast<cudaStream_t>(stream);

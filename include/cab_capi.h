@@ -80,6 +80,13 @@ CAB_API int cab_device_supported(int device);
  * CAB_ERR_LAUNCH if a kernel found its shared-memory layout did not fit and did nothing). */
 CAB_API int cab_device_status(void* stream, int* status);
 
+/* Failure-detection self-test (no reference counterpart): launches a kernel whose one
+ * bounded wait can never be satisfied; after `limit_us` microseconds it gives up exactly
+ * as the library's kernels do on a timeout (device status word := timeout, *gave_up_device
+ * := 1 in device memory) and returns. Nothing faults, traps or hangs; the next
+ * cab_device_status on `stream` reports CAB_ERR_TIMEOUT and the context stays usable. */
+CAB_API int cab_selftest_wait_timeout(int64_t limit_us, int* gave_up_device, void* stream);
+
 /*
  * Max-L2 coarsening: for every `block_size`-token block of q [B,Hq,N,D] and
  * k [B,Hkv,N,D], pick the token with the largest L2 norm (norm^2 accumulated in fp64;

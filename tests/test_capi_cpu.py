@@ -92,3 +92,14 @@ def test_ops_refuse_cpu_tensors():
     q = torch.randn(1, 1, 64, 64)
     with pytest.raises(RuntimeError, match="CUDA"):
         coarsen_qk_max_l2(q, q)
+
+
+def test_roofline_formulas_match_the_documented_sizes():
+    from cab_attention import roofline as rl
+    # north_star: 1065 MB coarsening, 16.4 + 256 GFLOP FRC, 269 MB top-k, 6.71 TFLOP attention
+    assert abs(rl.coarsen_bytes(2, 8, 8, 128000, 128) / 1e6 - 1065) < 1
+    assert abs(rl.frc_flops(2, 8, 2000, 128) / 1e9 - 272.4) < 0.1
+    assert abs(rl.topk_bytes(2, 8, 2000, 100) / 1e6 - 268.9) < 0.1
+    assert abs(rl.sparse_attention_flops(3_200_000, 64, 128) / 1e12 - 6.71) < 0.01
+    achieved, frac = rl.fraction(1065e6, 0.2, 6456.5, "GB/s")
+    assert abs(achieved - 5325) < 1 and 0.8 < frac < 0.85

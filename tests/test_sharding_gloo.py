@@ -86,3 +86,31 @@ def test_sharded_oracle_layer_equals_single_process():
     want = want.reshape(B * H, N, D)
     for r in range(world):
         np.testing.assert_allclose(results[r], want, rtol=1e-12, atol=1e-12)
+
+
+def _failing_worker(rank, world, port, result_q):
+    """Rank 1 dies before the gather; rank 0's gather must end with an error (the process
+    group timeout), not hang."""
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(3)  # the rank leaves between steps, with nothing of its own in flight
+    try:
+        sharding.gather_units(torch.zeros(1, 4), 2)
+        result_q.put(("no error", rank))
+    except Exception as e:  # noqa: BLE001 - the failure mode is what is tested
+        result_q.put((type(e).__name__, rank))
+
+
+def test_dead_rank_is_detected_not_hung():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    kind, rank = q.get(timeout=60)
+    for p in procs:
+        p.join(timeout=60)
+    assert rank == 0 and kind != "no error"
