@@ -741,27 +741,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(abort_flag) != 0)) { alive = false; break; }
       const float l_row = l + xs[(kb ^ 1) * 128 + r];
       const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
+      // O is read into registers and released at once (the next item's first PV may then
+      // overwrite it) before the conversion and the global stores
+      uint32_t o[kHalfD];
 #pragma unroll
-      for (int c = 0; c < kHalfD; c += 16) {
-        uint32_t o[16];
-        tmem_ld16(tmem_o + lane_addr + kb * kHalfD + c, o);
-        tmem_wait_ld();
-        if (row < p.Nq) {
+      for (int c = 0; c < kHalfD; c += 16)
+        tmem_ld16(tmem_o + lane_addr + kb * kHalfD + c, *reinterpret_cast<uint32_t(*)[16]>(&o[c]));
+      tmem_wait_ld();
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_free);
+      if (row < p.Nq) {
 #pragma unroll
-          for (int x = 0; x < 16; x += 8) {
-            uint32_t wv[4];
+        for (int c = 0; c < kHalfD; c += 8) {
+          uint32_t wv[4];
 #pragma unroll
-            for (int y = 0; y < 4; ++y)
-              wv[y] = pack2<kBF16>(__uint_as_float(o[x + 2 * y]) * inv, __uint_as_float(o[x + 2 * y + 1]) * inv);
-            *reinterpret_cast<uint4*>(orow + c + x) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-          }
+          for (int y = 0; y < 4; ++y)
+            wv[y] = pack2<kBF16>(__uint_as_float(o[c + 2 * y]) * inv, __uint_as_float(o[c + 2 * y + 1]) * inv);
+          *reinterpret_cast<uint4*>(orow + c) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
         }
       }
       if (row < p.Nq && p.lse && kb == 0)
         p.lse[static_cast<int64_t>(bh) * p.Nq + row] = l_row > 0.f ? (m_run + __log2f(l_row)) * kLn2 : -INFINITY;
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(o_free);
       if constexpr (kDense) {
         // Flush this CTA's private column sums into the caller's scores when the next item
         // belongs to another (b, h) (or there is none), and clear them.
