@@ -158,6 +158,10 @@ struct Cfg {
   static constexpr int kKStages = D == 128 ? 2 : 5;
   static constexpr int kVStages = D == 128 ? 3 : 5;
   static constexpr int kTileBytes = kQStages * kQBytes + kKStages * kKBytes + kVStages * kVBytes;
+  // sparse epilogue: each softmax warp stages its 32 rows x D/2 columns of O (one TMA store
+  // box) in the item's Q buffer; the eight boxes fill it exactly
+  static constexpr int kWarpOBytes = 32 * (D / 2) * 2;
+  static_assert(8 * kWarpOBytes == kQBytes, "O staging must fill the Q buffer");
   static constexpr int kSlotBytes = kDense ? 2 * 2 * 4 * 32 * 8 : 0;  // column sums [parity][kb][quad][lane] float2
   static constexpr int kXchgBytes = 2 * 2 * 128 * 4 + kSlotBytes;  // + row-max / row-sum exchange [parity][kb][row]
   static constexpr int kAuxBytes = kXchgBytes + 512;   // + mbarriers (<= 54), TMEM slot, abort flag, counter
@@ -230,7 +234,7 @@ __device__ __forceinline__ int item_tiles(const Params& p, int64_t item) {
     const int pr = static_cast<int>(item % p.P);
     return p.causal ? min(p.Tk, pr + 1) : p.Tk;
   } else {
-    return __ldg(p.ntiles + item);
+    return static_cast<int>(ld_nc_u32(p.ntiles + item));
   }
 }
 
@@ -257,7 +261,8 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 template <int D, bool kBF16, bool kDense>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-                   const __grid_constant__ CUtensorMap vmap, const Params p) {
+                   const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap omap,
+                   const Params p) {
   using C = Cfg<D, kDense>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -301,7 +306,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     prefetch_tensormap(&qmap);
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
-    for (int s = 0; s < C::kQStages; ++s) { mbar_init(&q_full[s], 1); mbar_init(&q_empty[s], 1); }
+    if (!kDense) prefetch_tensormap(&omap);
+    // sparse: a Q buffer is free once the item's S MMAs have completed and each softmax
+    // warp's O store has read its staged box out of it
+    for (int s = 0; s < C::kQStages; ++s) { mbar_init(&q_full[s], 1); mbar_init(&q_empty[s], kDense ? 1 : 1 + kSoftmaxWarps); }
     for (int s = 0; s < C::kKStages; ++s) { mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1); }
     for (int s = 0; s < C::kVStages; ++s) { mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1); }
     for (int s = 0; s < kSBufs; ++s) { mbar_init(&s_full[s], 1); mbar_init(&buf_free[s], 1); }
@@ -332,12 +340,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (lane == 0) {
       uint32_t gi = 0, kt = 0, vt = 0;
       bool ok = true;
+      // Tile counts are read one item ahead and list entries one tile ahead, so no list
+      // read sits between a free stage and its TMA issue.
+      int T_next = static_cast<int64_t>(blockIdx.x) < p.items ? item_tiles<kDense>(p, blockIdx.x) : 0;
       for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
-        const int T = item_tiles<kDense>(p, item);
+        const int T = T_next;
+        if (item + gridDim.x < p.items) T_next = item_tiles<kDense>(p, item + gridDim.x);
         if (T == 0) continue;
-        const int bh = static_cast<int>(item / p.P), pr = static_cast<int>(item % p.P);
+        const uint32_t it = static_cast<uint32_t>(item);
+        const int bh = static_cast<int>(it / static_cast<uint32_t>(p.P));
+        const int pr = static_cast<int>(it - static_cast<uint32_t>(bh) * static_cast<uint32_t>(p.P));
         const int b = bh / p.Hq, h = bh % p.Hq, hk = h / G;
         const uint32_t* ul = p.ulist + item * p.stride;
+        uint32_t e0 = 0u, e1 = 0u;
+        if constexpr (!kDense) {
+          e0 = ld_nc_u32(ul);
+          e1 = ld_nc_u32(ul + 1);
+        }
         const int qs = static_cast<int>(gi % C::kQStages);
         if (!mbar_wait(&q_empty[qs], ((gi / C::kQStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
         mbar_arrive_expect_tx(&q_full[qs], C::kQBytes);
@@ -346,8 +365,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tma_load_4d(sQ + qs * C::kQBytes + a * 16384, &qmap, &q_full[qs], 64 * a, 128 * pr, h, b);
         ++gi;
         for (int t = 0; t < T; ++t) {
-          const int j0 = static_cast<int>(item_entry<kDense>(ul, t, 0) & kIdxMask);
-          const int j1 = static_cast<int>(item_entry<kDense>(ul, t, 1) & kIdxMask);
+          const int j0 = kDense ? 2 * t : static_cast<int>(e0 & kIdxMask);
+          const int j1 = kDense ? 2 * t + 1 : static_cast<int>(e1 & kIdxMask);
+          if constexpr (!kDense) {
+            if (t + 1 < T) {
+              e0 = ld_nc_u32(ul + 2 * t + 2);
+              e1 = ld_nc_u32(ul + 2 * t + 3);
+            }
+          }
           const int ks = kt % C::kKStages;
           if (!mbar_wait(&k_empty[ks], ((kt / C::kKStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&k_full[ks], C::kKBytes);
@@ -386,8 +411,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint64_t dK = make_smem_desc(smem_u32(sK), 16, 1024, 2);
       uint32_t gi = 0, kt = 0, gt = 0;
       bool ok = true;
+      int T_next = static_cast<int64_t>(blockIdx.x) < p.items ? item_tiles<kDense>(p, blockIdx.x) : 0;
       for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
-        const int T = item_tiles<kDense>(p, item);
+        const int T = T_next;
+        if (item + gridDim.x < p.items) T_next = item_tiles<kDense>(p, item + gridDim.x);
         if (T == 0) continue;
         const int qs = static_cast<int>(gi % C::kQStages);
         if (!mbar_wait(&q_full[qs], (gi / C::kQStages) & 1, abort_flag)) { ok = false; break; }
@@ -430,8 +457,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint64_t dV = make_smem_desc(smem_u32(sV), 16384, 1024, 2);
       uint32_t gi = 0, vt = 0, gt = 0;
       bool ok = true;
+      int T_next = static_cast<int64_t>(blockIdx.x) < p.items ? item_tiles<kDense>(p, blockIdx.x) : 0;
       for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
-        const int T = item_tiles<kDense>(p, item);
+        const int T = T_next;
+        if (item + gridDim.x < p.items) T_next = item_tiles<kDense>(p, item + gridDim.x);
         if (T == 0) continue;
         for (int t = 0; t < T; ++t) {
           // P from TMEM (in its S buffer), V from shared memory (MN-major)
@@ -467,8 +496,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (lane == 0) {
       uint32_t gt = 0;
       bool ok = true;
+      int T_next = static_cast<int64_t>(blockIdx.x) < p.items ? item_tiles<kDense>(p, blockIdx.x) : 0;
       for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
-        const int T = item_tiles<kDense>(p, item);
+        const int T = T_next;
+        if (item + gridDim.x < p.items) T_next = item_tiles<kDense>(p, item + gridDim.x);
         for (int t = 0; t < T; ++t) {
           const uint32_t g = gt + t;
           if (!mbar_wait(&o_ready[g & 1], (g >> 1) & 1, abort_flag)) { ok = false; break; }
@@ -509,9 +540,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     uint32_t e_first_next = 0u;
     if (static_cast<int64_t>(blockIdx.x) < p.items) {
       T_next = item_tiles<kDense>(p, blockIdx.x);
-      e_first_next = kDense ? item_entry<kDense>(nullptr, 0, kb) : __ldg(p.ulist + static_cast<int64_t>(blockIdx.x) * p.stride + kb);
+      e_first_next = kDense ? item_entry<kDense>(nullptr, 0, kb) : ld_nc_u32(p.ulist + static_cast<int64_t>(blockIdx.x) * p.stride + kb);
     }
     int dense_tiles_seen = 0;  // dense + column sums: key tiles touched in this CTA's private buffer
+    uint32_t gq = 0;   // items with tiles so far (their Q buffers alternate like the producer's)
+    int pend_q = -1;   // sparse: Q buffer holding this warp's O box until its store has read it
     for (int64_t item = blockIdx.x; item < p.items; item += gridDim.x) {
       const int T = T_next;
       const uint32_t e_first = e_first_next;
@@ -519,10 +552,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int64_t nitem = item + gridDim.x;
         if (nitem < p.items) {
           T_next = item_tiles<kDense>(p, nitem);
-          e_first_next = kDense ? item_entry<kDense>(nullptr, 0, kb) : __ldg(p.ulist + nitem * p.stride + kb);
+          e_first_next = kDense ? item_entry<kDense>(nullptr, 0, kb) : ld_nc_u32(p.ulist + nitem * p.stride + kb);
         }
       }
-      const int bh = static_cast<int>(item / p.P), pr = static_cast<int>(item % p.P);
+      const uint32_t it = static_cast<uint32_t>(item);
+      const int bh = static_cast<int>(it / static_cast<uint32_t>(p.P));
+      const int pr = static_cast<int>(it - static_cast<uint32_t>(bh) * static_cast<uint32_t>(p.P));
       const int b = bh / p.Hq, h = bh % p.Hq;
       const int row = 128 * pr + r;
       const int64_t ooff = b * p.o_s0 + h * p.o_s1 + static_cast<int64_t>(row) * p.o_s2;
@@ -540,6 +575,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       float m_exact = -INFINITY;  // dense column scores: exact running max (log2 units)
       bool ok = true;
       uint32_t e_next = e_first;
+      if constexpr (!kDense) {
+        // hand the previous item's Q buffer back to the producer once this warp's O store
+        // has read its staged box (kept out of the tile loop, whose code it would slow)
+        if (pend_q >= 0) {
+          if (lane == 0) {
+            bulk_wait_read_all();
+            mbar_arrive(&q_empty[pend_q]);
+          }
+          pend_q = -1;
+        }
+      }
       for (int t = 0; t < T; ++t) {
         const uint32_t g = gt + t, buf = g % kSBufs;
         const uint32_t e = e_next;
@@ -751,16 +797,46 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(o_free);
-      if (row < p.Nq) {
+      if constexpr (kDense) {
+        if (row < p.Nq) {
 #pragma unroll
-        for (int c = 0; c < kHalfD; c += 8) {
+          for (int c = 0; c < kHalfD; c += 8) {
+            uint32_t wv[4];
+#pragma unroll
+            for (int y = 0; y < 4; ++y)
+              wv[y] = pack2<kBF16>(__uint_as_float(o[c + 2 * y]) * inv, __uint_as_float(o[c + 2 * y + 1]) * inv);
+            *reinterpret_cast<uint4*>(orow + c) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          }
+        }
+      } else {
+        // O / l goes through this item's Q buffer, whose last reader, S of the item's last
+        // tile, has completed (this warp waited for it): the warp stages its 32 rows x D/2
+        // columns in the output tensor map's swizzled box layout (16-byte chunk c of row x
+        // at chunk c ^ (x & 7) for 128-byte rows, c ^ ((x >> 1) & 3) for 64-byte rows) and
+        // lane 0 writes the box with one TMA store; rows past the sequence end are clipped
+        // by the tensor map. Coalesced, and the warp moves on without waiting for it.
+        constexpr int kRowBytes = kHalfD * 2;
+        const int qs = static_cast<int>(gq % C::kQStages);
+        uint8_t* wbox = sQ + qs * C::kQBytes + (quad + 4 * kb) * C::kWarpOBytes;
+        const int swz = kRowBytes == 128 ? (lane & 7) : ((lane >> 1) & 3);
+#pragma unroll
+        for (int c = 0; c < kHalfD / 8; ++c) {
           uint32_t wv[4];
 #pragma unroll
           for (int y = 0; y < 4; ++y)
-            wv[y] = pack2<kBF16>(__uint_as_float(o[c + 2 * y]) * inv, __uint_as_float(o[c + 2 * y + 1]) * inv);
-          *reinterpret_cast<uint4*>(orow + c) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            wv[y] = pack2<kBF16>(__uint_as_float(o[8 * c + 2 * y]) * inv, __uint_as_float(o[8 * c + 2 * y + 1]) * inv);
+          *reinterpret_cast<uint4*>(wbox + lane * kRowBytes + 16 * (c ^ swz)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
         }
+        fence_proxy_async_smem();
+        __syncwarp();
+        const int row0 = 128 * pr + 32 * quad;
+        if (lane == 0 && row0 < p.Nq) {
+          tma_store_4d(&omap, wbox, kb * kHalfD, row0, h, b);
+          bulk_commit_group();
+        }
+        pend_q = qs;
       }
+      ++gq;
       if (row < p.Nq && p.lse && kb == 0)
         p.lse[static_cast<int64_t>(bh) * p.Nq + row] = l_row > 0.f ? (m_run + __log2f(l_row)) * kLn2 : -INFINITY;
       if constexpr (kDense) {
@@ -787,6 +863,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       gt += T;
     }
     if (!alive) named_bar_arrive(pair_bar, 64);  // release a partner blocked at the pair barrier
+    if (!kDense && lane == 0) bulk_wait_all();  // the staged boxes stay valid until stored
   }
   tc_fence_before_sync();
   __syncthreads();
@@ -911,23 +988,25 @@ static bool use_tensor_cores(int dtype, int64_t D, int64_t bs) {
 }
 
 template <int D, bool kBF16, bool kDense>
-static int launch_tc(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const Params& p,
-                     int grid, cudaStream_t st) {
+static int launch_tc(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const CUtensorMap& om,
+                     const Params& p, int grid, cudaStream_t st) {
   auto kern = attn_tc_kernel<D, kBF16, kDense>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D, kDense>::kSmem);
-  kern<<<grid, kAttnThreads, Cfg<D, kDense>::kSmem, st>>>(qm, km, vm, p);
+  kern<<<grid, kAttnThreads, Cfg<D, kDense>::kSmem, st>>>(qm, km, vm, om, p);
   return check_launch("attn_tc_kernel");
 }
 
-// Q / K / V / O tensor map over [B, H, rows, D] with {b, h, n} strides in elements.
+// Q / K / V / O tensor map over [B, H, rows, D] with {b, h, n} strides in elements; the
+// box is box_cols x box_rows (64 columns = one 128-byte swizzle atom for Q, K and V).
 static int attn_tensor_map(CUtensorMap* m, const void* ptr, int64_t B, int64_t H, int64_t rows, int64_t D,
-                           const int64_t* s, size_t es, int dtype, uint32_t box_rows) {
+                           const int64_t* s, size_t es, int dtype, uint32_t box_rows, uint32_t box_cols = 64,
+                           CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(rows), static_cast<uint64_t>(H),
                       static_cast<uint64_t>(B)};
   uint64_t str[3] = {static_cast<uint64_t>(s[2]) * es, static_cast<uint64_t>(s[1]) * es,
                      static_cast<uint64_t>(s[0]) * es};
-  uint32_t box[4] = {64, box_rows, 1, 1};
-  return make_tensor_map(m, tma_type(dtype), 4, ptr, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  uint32_t box[4] = {box_cols, box_rows, 1, 1};
+  return make_tensor_map(m, tma_type(dtype), 4, ptr, dims, str, box, swz);
 }
 
 // Dense (flash) forward: CTAs in the launch and the private column-buffer stride.
@@ -984,6 +1063,7 @@ extern "C" int cab_sparse_attn_fwd(const void* q, const void* k, const void* v, 
 
   if (use_tensor_cores(dtype, D, block_size)) {
     const WsLayout L = ws_layout(B, Hq, N, block_size, kmax);
+    if (L.items >= (int64_t)1 << 31) return fail(CAB_ERR_UNSUPPORTED, "attn: more than 2^31 query-block pairs");
     if (!workspace || workspace_bytes < L.total)
       return fail(CAB_ERR_WORKSPACE, "attn: workspace of %zu bytes needed, %zu given", L.total, workspace_bytes);
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(workspace))
@@ -1012,10 +1092,14 @@ extern "C" int cab_sparse_attn_fwd(const void* q, const void* k, const void* v, 
     pair_union_kernel<<<ugrid, 128, usmem, st>>>(up);
     if (int rc = check_launch("pair_union_kernel")) return rc;
 
-    CUtensorMap qm{}, km{}, vm{};
+    CUtensorMap qm{}, km{}, vm{}, om{};
     if (int rc = attn_tensor_map(&qm, q, B, Hq, N, D, q_strides, es, dtype, 128)) return rc;
     if (int rc = attn_tensor_map(&km, k, B, Hkv, N, D, k_strides, es, dtype, 64)) return rc;
     if (int rc = attn_tensor_map(&vm, v, B, Hkv, N, D, v_strides, es, dtype, 64)) return rc;
+    // output: one 32-row x D/2 box per softmax warp (128-byte rows for D=128, 64-byte for 64)
+    if (int rc = attn_tensor_map(&om, out, B, Hq, N, D, o_strides, es, dtype, 32, static_cast<uint32_t>(D / 2),
+                                 D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
+      return rc;
     Params p{};
     p.B = static_cast<int32_t>(B);
     p.Hq = static_cast<int32_t>(Hq);
@@ -1042,8 +1126,8 @@ extern "C" int cab_sparse_attn_fwd(const void* q, const void* k, const void* v, 
     const bool bf = dtype == CAB_DTYPE_BF16;
     const int grid = static_cast<int>(std::min<int64_t>(p.items, current_sm_count()));
     if (D == 128)
-      return bf ? launch_tc<128, true, false>(qm, km, vm, p, grid, st) : launch_tc<128, false, false>(qm, km, vm, p, grid, st);
-    return bf ? launch_tc<64, true, false>(qm, km, vm, p, grid, st) : launch_tc<64, false, false>(qm, km, vm, p, grid, st);
+      return bf ? launch_tc<128, true, false>(qm, km, vm, om, p, grid, st) : launch_tc<128, false, false>(qm, km, vm, om, p, grid, st);
+    return bf ? launch_tc<64, true, false>(qm, km, vm, om, p, grid, st) : launch_tc<64, false, false>(qm, km, vm, om, p, grid, st);
   }
 
   if (block_size > 128 || D > 128)
@@ -1114,6 +1198,7 @@ extern "C" int cab_flash_attn_fwd(const void* q, const void* k, const void* v, v
       if (ss[x][i] <= 0 || (ss[x][i] * static_cast<int64_t>(es)) % 16 != 0)
         return fail(CAB_ERR_INVALID_ARG, "flash: strides must be positive multiples of 16 bytes");
   const FlashLayout L = flash_layout(B, Hq, Nq, Nk);
+  if (L.items >= (int64_t)1 << 31) return fail(CAB_ERR_UNSUPPORTED, "flash: more than 2^31 query tiles");
   if (scores) {
     if (!workspace || workspace_bytes < L.partial_bytes)
       return fail(CAB_ERR_WORKSPACE, "flash: workspace of %zu bytes needed, %zu given", L.partial_bytes, workspace_bytes);
@@ -1156,6 +1241,6 @@ extern "C" int cab_flash_attn_fwd(const void* q, const void* k, const void* v, v
   p.pstride = L.pstride;
   const bool bf = dtype == CAB_DTYPE_BF16;
   if (D == 128)
-    return bf ? launch_tc<128, true, true>(qm, km, vm, p, L.grid, st) : launch_tc<128, false, true>(qm, km, vm, p, L.grid, st);
-  return bf ? launch_tc<64, true, true>(qm, km, vm, p, L.grid, st) : launch_tc<64, false, true>(qm, km, vm, p, L.grid, st);
+    return bf ? launch_tc<128, true, true>(qm, km, vm, qm, p, L.grid, st) : launch_tc<128, false, true>(qm, km, vm, qm, p, L.grid, st);
+  return bf ? launch_tc<64, true, true>(qm, km, vm, qm, p, L.grid, st) : launch_tc<64, false, true>(qm, km, vm, qm, p, L.grid, st);
 }
