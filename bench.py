@@ -73,54 +73,116 @@ def measured_peaks():
 
 # --------------------------------------------------------------------------- clocks
 class ClockSampler:
+    """SM clock, power and clock-event (throttle) reasons of this rank's GPU, read every
+    10 ms through NVML on a background thread (read-only queries); only the samples taken
+    between mark_start() and mark_end() -- wall clock around the synchronised timed
+    region -- are reported. Without NVML it falls back to nvidia-smi at 200 ms."""
+
+    REASONS = (("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20), ("hw_thermal_slowdown", 0x40),
+               ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80))
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, local_rank: int):
+        self.rank_dev = local_rank
+        self.samples = []  # (t, sm_mhz, reason bits or names, power_w)
+        self.t0 = self.t1 = None
+        self.max_mhz = None
         self.proc = None
-        self.lines = []
+        self.stop_flag = threading.Event()
+        self.thread = None
+        self.mode = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            pr = torch.cuda.get_device_properties(self.rank_dev)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.rank_dev)
 
     def start(self):
         try:
+            nv, h = self._nvml_handle()
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self.mode = "nvml"
+
+            def loop():
+                while not self.stop_flag.is_set():
+                    try:
+                        sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                        rs = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                        pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                        self.samples.append((time.monotonic(), sm, rs, pw))
+                    except Exception:
+                        pass
+                    time.sleep(0.01)
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.mode = None
+        try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                 "-lms", "200", "-i", str(self.rank_dev)], stdout=subprocess.PIPE,
                 stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.mode = "nvidia-smi"
+
+            def read():
+                names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+                for line in self.proc.stdout:
+                    parts = [x.strip() for x in line.strip().split(",")]
+                    if len(parts) < 8:
+                        continue
+                    try:
+                        sm, mx = float(parts[0]), float(parts[1])
+                    except ValueError:
+                        continue
+                    self.max_mhz = mx
+                    rs = {n for n, v in zip(names, parts[4:8]) if v.lower().startswith("active")}
+                    self.samples.append((time.monotonic(), sm, rs, None))
+            self.thread = threading.Thread(target=read, daemon=True)
             self.thread.start()
         except (OSError, FileNotFoundError):
             self.proc = None
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def mark_start(self):
+        self.t0 = time.monotonic()
+
+    def mark_end(self):
+        self.t1 = time.monotonic()
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 8:
-                continue
+        if self.mode is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
+        self.stop_flag.set()
+        if self.proc is not None:
+            self.proc.terminate()
             try:
-                sm.append(float(parts[0]))
-                mx = float(parts[1])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[4:8]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        t0 = self.t0 if self.t0 is not None else float("-inf")
+        t1 = self.t1 if self.t1 is not None else float("inf")
+        win = [x for x in list(self.samples) if t0 <= x[0] <= t1]
+        reasons = set()
+        for _, _, rs, _ in win:
+            if isinstance(rs, int):
+                reasons |= {n for n, bit in self.REASONS if rs & bit}
+            else:
+                reasons |= rs
+        pw = [x[3] for x in win if x[3] is not None]
+        out = {"sm_mhz": statistics.median(x[1] for x in win) if win else None, "sm_max_mhz": self.max_mhz,
+               "reasons": sorted(reasons), "samples": len(win), "source": self.mode}
+        if pw:
+            out["power_w_median"] = round(statistics.median(pw), 1)
+        return out
 
 
 # --------------------------------------------------------------------------- our arm
@@ -237,8 +299,9 @@ def run_ours(args, cfg, rank, world, local_rank):
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nstage)] for _ in range(args.steps)]
     sampler = ClockSampler(local_rank)
     sampler.start()
-    time.sleep(0.5)
+    time.sleep(0.2)
     barrier()
+    sampler.mark_start()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record()
@@ -246,6 +309,7 @@ def run_ours(args, cfg, rank, world, local_rank):
         out, kv_num = layer.stages(q, k, v, evs[s])
     end.record()
     barrier()
+    sampler.mark_end()
     clocks = sampler.stop()
     total_ms = start.elapsed_time(end)
     stage_ms = np.array([[evs[s][i].elapsed_time(evs[s][i + 1]) for i in range(nstage - 1)]
@@ -335,9 +399,9 @@ def run_ours(args, cfg, rank, world, local_rank):
 # dram__bytes_read.sum + dram__bytes_write.sum per attention launch from the committed ncu
 # capture (profiles/attn_tc_kernel_ns_4heads.md); None until a capture exists for the
 # workload. "ns": the capture ran the north_star shape at 4 of its 16 (batch, head) units
-# (408.579 MB read + 114.571 MB written); DRAM traffic is per-unit (each unit reads its own
+# (409.461 MB read + 116.139 MB written); DRAM traffic is per-unit (each unit reads its own
 # Q/K/V once and writes its own O), so the full launch is scaled by 16 / 4.
-ATTN_TRAFFIC_BYTES = {"ns": (408.579072e6 + 114.571264e6) * 4}
+ATTN_TRAFFIC_BYTES = {"ns": (409.461248e6 + 116.139264e6) * 4}
 
 
 # --------------------------------------------------------------------------- reference arm
@@ -405,9 +469,10 @@ def run_flash_ours(args, cfg, rank, world, local_rank):
     barrier()
     sampler = ClockSampler(local_rank)
     sampler.start()
-    time.sleep(0.5)
+    time.sleep(0.2)
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
     barrier()
+    sampler.mark_start()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for st in range(args.steps):
@@ -420,6 +485,7 @@ def run_flash_ours(args, cfg, rank, world, local_rank):
         flash_attention_forward(q, k, v, out=out)
         ev[st][1].record()
     barrier()
+    sampler.mark_end()
     clocks = sampler.stop()
     t = torch.tensor([start.elapsed_time(end)], device=dev, dtype=torch.float64)
     if world > 1:
@@ -595,8 +661,10 @@ def run_aux_ours(args, cfg, rank, world, local_rank):
             return keep.cpu(), counts.cpu()
         launches = 2
     sampler.start()
-    time.sleep(0.3)
+    time.sleep(0.2)
+    sampler.mark_start()
     ms = _time_device(fn, args.steps, args.warmup)
+    sampler.mark_end()
     clocks = sampler.stop()
     e2e = _time_device(e2e_fn, args.steps, 1)
     achieved = nbytes / ms / 1e6

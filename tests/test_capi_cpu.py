@@ -103,3 +103,21 @@ def test_roofline_formulas_match_the_documented_sizes():
     assert abs(rl.sparse_attention_flops(3_200_000, 64, 128) / 1e12 - 6.71) < 0.01
     achieved, frac = rl.fraction(1065e6, 0.2, 6456.5, "GB/s")
     assert abs(achieved - 5325) < 1 and 0.8 < frac < 0.85
+
+
+def test_clock_sampler_reports_only_the_timed_window():
+    """bench.py's clock record: samples outside [mark_start, mark_end] (the idle lead-in
+    and tail) are dropped, NVML reason bits map to their names."""
+    import sys
+    import time
+    sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+    import bench
+    s = bench.ClockSampler(0)
+    s.mode, s.max_mhz = "nvml", 1965.0
+    now = time.monotonic()
+    s.samples = [(now - 1.0, 1965.0, 0, 100.0), (now + 0.1, 1500.0, 0x4, 990.0),
+                 (now + 0.2, 1520.0, 0x4 | 0x8, 995.0), (now + 5.0, 1965.0, 0, 120.0)]
+    s.t0, s.t1 = now, now + 1.0
+    c = s.stop()
+    assert c["samples"] == 2 and c["sm_mhz"] == 1510.0 and c["sm_max_mhz"] == 1965.0
+    assert c["reasons"] == ["hw_slowdown", "sw_power_cap"]
