@@ -58,7 +58,12 @@ CONFIGS = {
     "flash": dict(B=1, Hq=8, Hkv=8, N=32768, D=128, sparsity=0.0, causal=False,
                   workload="flash attention + cumulative column scores: B1 H8 N32768 D128 bf16, "
                            "non-causal (flash_attention_with_cumulative_scores)"),
+    # predictor-only latency per N (the line's value is the largest N)
+    "sweep": dict(B=2, Hq=8, Hkv=8, N=131072, D=128, sparsity=0.95, causal=False,
+                  workload="configs[3]: CoarseCurvaturePredictor over N in {1k, 4k, 16k, 64k, 128k}, "
+                           "B2 H8 D128 bf16, s=0.95"),
 }
+SWEEP_N = (1024, 4096, 16384, 65536, 131072)
 BLOCK = 64
 LAMBDA = 0.5
 
@@ -439,6 +444,164 @@ def run_reference(args, cfg):
     }
 
 
+# --------------------------------------------------------------------------- predictor sweep
+def run_sweep_ours(args, cfg, rank, world, local_rank):
+    """the predictor (coarsen -> FRC -> top-k) per N on device-resident q, k.
+    Each N is timed over `steps` steps with CUDA events per stage; the line's value and
+    roofline are those of the largest N, the others are in `sweep`."""
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    from cab_attention import CoarseCurvaturePredictor, _lib
+    from cab_attention import roofline as rl
+    from cab_attention.kernels import coarsen_qk_max_l2, compute_block_frc, topk_blocks
+    hbm, tf_burst, tf_sus, peak_kind = measured_peaks()
+    pred = CoarseCurvaturePredictor(block_size=BLOCK, sparsity=cfg["sparsity"], lambda_redundancy=LAMBDA)
+    B, Hq, Hkv, D = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"]
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.2)
+    sweep, last = {}, None
+    for N in SWEEP_N:
+        c = dict(cfg, N=N)
+        q_h, k_h, _ = make_inputs(c, rank, args.seed, pin=True)
+        q, k = q_h.to(dev), k_h.to(dev)
+        kk = pred.keep_per_row(N)
+
+        def step(ev=None):
+            if ev: ev[0].record()
+            qc, kc = coarsen_qk_max_l2(q, k, BLOCK)
+            if ev: ev[1].record()
+            frc, _, _ = compute_block_frc(qc, kc, 1.0, LAMBDA, return_affinity=False, return_redundancy=False)
+            if ev: ev[2].record()
+            idx, num, _ = topk_blocks(frc, kk, True, True, False, return_dense=False)
+            if ev: ev[3].record()
+            return idx, num
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        assert _lib.device_status() == 0
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+        barrier()
+        if N == SWEEP_N[-1]:
+            sampler.mark_start()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for st in range(args.steps):
+            step(evs[st])
+        end.record()
+        barrier()
+        if N == SWEEP_N[-1]:
+            sampler.mark_end()
+        t = torch.tensor([start.elapsed_time(end)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        st_ms = [statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.steps))
+                 for j in range(3)]
+        M = (N + BLOCK - 1) // BLOCK
+        sweep[str(N)] = {"ms": t.item() / args.steps, "M": M, "k": kk, "coarsen_ms": st_ms[0],
+                         "frc_ms": st_ms[1], "topk_ms": st_ms[2]}
+        last = (N, M, kk, q_h, k_h, q, k, step, st_ms)
+    clocks = sampler.stop()
+
+    N, M, kk, q_h, k_h, q, k, step, st_ms = last
+    # end to end at the largest N: pinned q, k in, block lists out, every step
+    idx_h = torch.empty(B, Hq, M, kk, dtype=torch.int32).pin_memory()
+    num_h = torch.empty(B, Hq, M, dtype=torch.int32).pin_memory()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        qd, kd = q_h.to(dev, non_blocking=True), k_h.to(dev, non_blocking=True)
+        idx, num = pred.predict_blocks(qd, kd)
+        idx_h.copy_(idx, non_blocking=True)
+        num_h.copy_(num, non_blocking=True)
+    e1.record()
+    barrier()
+    te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    c_ms, f_ms, k_ms = st_ms
+    flop = rl.frc_flops(B, Hq, M, D)
+    achieved = flop / f_ms / 1e9
+    stages = {
+        "coarsen": {"ms": c_ms, "GB/s": rl.coarsen_bytes(B, Hq, Hkv, N, D, 2, BLOCK) / c_ms / 1e6},
+        "frc": {"ms": f_ms, "TFLOP/s": achieved},
+        "topk": {"ms": k_ms, "GB/s": rl.topk_bytes(B, Hq, M, kk) / k_ms / 1e6},
+    }
+    if rank != 0:
+        return None
+    cpu = None
+    if world == 1 and args.cpu_baseline_seconds > 0:
+        ms, desc = sweep_cpu_sample(dict(cfg, N=N), args.seed)
+        cpu = {"value": ms, "unit": "ms", "cores": os.cpu_count(), "kind": "port", "sample": desc}
+    return {
+        "metric": "CAB predictor ms @N=128k (sweep over N)",
+        "value": sweep[str(N)]["ms"] / world, "unit": "ms", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": sweep[str(N)]["ms"], "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (iid N(0,1) per-(b,h) seeded Q/K)",
+        "config": {"workload": cfg["workload"], "per_rank": f"B={B} Hq={Hq} Hkv={Hkv} D={D}",
+                   "parallelism": f"(batch x head) shards, {world} rank(s), no data-path collective",
+                   "l2": "q, k at N=128k: 537 MB per rank > 126 MB L2; no flush needed"},
+        "sweep": sweep,
+        "stages": stages,
+        "roofline": {"bound": "tensor", "kernel": "frc::gemm_kernel (A = Qc Kc^T, T = Direct Direct + F epilogue)",
+                     "achieved": achieved, "peak": tf_burst, "unit": "TFLOP/s", "frac": achieved / tf_burst,
+                     "peak_source": f"{peak_kind} bf16_tflops (burst: the GEMMs are timed alone)",
+                     "traffic": None},
+        "cpu_baseline": cpu,
+        "e2e": {"value": te.item() / args.steps / world, "unit": "ms",
+                "h2d_bytes_per_step": world * (q_h.numel() + k_h.numel()) * q_h.element_size(),
+                "d2h_bytes_per_step": world * (idx_h.numel() + num_h.numel()) * 4},
+        "gpu_launches": 4 * args.steps,
+        "clocks": clocks,
+    }
+
+
+def sweep_cpu_sample(cfg, seed=0):
+    """The numpy oracle predictor of one (b, h) head at N, scaled by the heads of the layer."""
+    from oracle import cab_oracle as orc
+    from cab_attention import synthetic
+    N, D = cfg["N"], cfg["D"]
+    M = (N + BLOCK - 1) // BLOCK
+    q = synthetic.normal_heads("q", [0], 1, N, D, torch.bfloat16, seed).float().numpy()
+    k = synthetic.normal_heads("k", [0], 1, N, D, torch.bfloat16, seed).float().numpy()
+    t0 = time.perf_counter()
+    orc.predictor(q, k, BLOCK, cfg["sparsity"], LAMBDA)
+    dt = time.perf_counter() - t0
+    heads = cfg["B"] * cfg["Hq"]
+    return dt * 1e3 * heads, (f"numpy oracle predictor of 1 of {heads} heads at N={N} (M={M}) "
+                              f"({dt:.2f} s), scaled by the heads")
+
+
+def run_sweep_reference(args, cfg):
+    """The reference path's CPU restatement of the predictor (oracle port) per N."""
+    sweep = {}
+    for N in SWEEP_N:
+        vals, desc = [], ""
+        for _ in range(max(1, args.steps)):
+            ms, desc = sweep_cpu_sample(dict(cfg, N=N), args.seed)
+            vals.append(ms)
+        sweep[str(N)] = {"ms": statistics.median(vals)}
+    value = sweep[str(SWEEP_N[-1])]["ms"]
+    return {
+        "metric": "CAB predictor ms @N=128k (sweep over N)", "impl": "reference", "value": value,
+        "unit": "ms", "n_gpus": 0, "steps": args.steps, "warmup": 0, "ms_per_step": value,
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (iid N(0,1) per-(b,h) seeded Q/K)", "config": {"workload": cfg["workload"]},
+        "sweep": sweep,
+        "cpu_baseline": {"value": value, "unit": "ms", "cores": os.cpu_count(), "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
 # --------------------------------------------------------------------------- flash row
 def flash_flop(cfg):
     from cab_attention import roofline as rl
@@ -746,6 +909,8 @@ def main():
             torch.set_num_threads(os.cpu_count())
             if args.config == "flash":
                 res = run_flash_reference(args, cfg)
+            elif args.config == "sweep":
+                res = run_sweep_reference(args, cfg)
             elif args.config in ("nodefrc", "evict"):
                 res = run_aux_reference(args, cfg)
             else:
@@ -758,7 +923,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run = {"flash": run_flash_ours, "nodefrc": run_aux_ours, "evict": run_aux_ours}.get(args.config, run_ours)
+        run = {"flash": run_flash_ours, "nodefrc": run_aux_ours, "evict": run_aux_ours,
+               "sweep": run_sweep_ours}.get(args.config, run_ours)
         res = run(args, cfg, rank, world, local_rank)
         if rank == 0 and res is not None:
             print(json.dumps(res), flush=True)
