@@ -58,6 +58,10 @@ CONFIGS = {
     "flash": dict(B=1, Hq=8, Hkv=8, N=32768, D=128, sparsity=0.0, causal=False,
                   workload="flash attention + cumulative column scores: B1 H8 N32768 D128 bf16, "
                            "non-causal (flash_attention_with_cumulative_scores)"),
+    # the CABAttention layer at the README scale (D = dim / heads = 64)
+    "c3": dict(B=2, Hq=8, Hkv=8, N=128000, D=64, dim=512, sparsity=0.95, causal=False,
+               workload="configs[2]: CABAttention(dim=512, heads=8, head_dim=64) B2 N128000 bf16, s=0.95, "
+                        "projection weights N(0, 0.02^2)"),
     # predictor-only latency per N (the line's value is the largest N)
     "sweep": dict(B=2, Hq=8, Hkv=8, N=131072, D=128, sparsity=0.95, causal=False,
                   workload="configs[3]: CoarseCurvaturePredictor over N in {1k, 4k, 16k, 64k, 128k}, "
@@ -410,18 +414,19 @@ ATTN_TRAFFIC_BYTES = {"ns": (409.461248e6 + 116.139264e6) * 4}
 
 
 # --------------------------------------------------------------------------- reference arm
-def run_reference(args, cfg):
+def run_reference(args, cfg, sampler=None, metric="CAB layer ms @N=128k (predictor + sparse attn)"):
     """The reference path's CPU restatement (oracle port), bounded sample per step."""
+    sampler = sampler or cpu_sample
     budget = max(2.0, args.reference_step_seconds)
     for _ in range(args.warmup):
-        cpu_sample(cfg, budget, args.seed)
+        sampler(cfg, budget, args.seed)
     vals, desc = [], ""
     for _ in range(args.steps):
-        ms, desc = cpu_sample(cfg, budget, args.seed)
+        ms, desc = sampler(cfg, budget, args.seed)
         vals.append(ms)
     value = statistics.median(vals)
     return {
-        "metric": "CAB layer ms @N=128k (predictor + sparse attn)",
+        "metric": metric,
         "impl": "reference",
         "value": value,
         "unit": "ms",
@@ -442,6 +447,151 @@ def run_reference(args, cfg):
                  "cab_attention / kernels modules are listed in its README but absent), so its "
                  "CPU restatement under oracle/ is timed"),
     }
+
+
+# --------------------------------------------------------------------------- CABAttention layer
+def _c3_layer(cfg, seed, dev):
+    from cab_attention import CABAttention
+    layer = CABAttention(cfg["dim"], cfg["Hq"], block_size=BLOCK, sparsity=cfg["sparsity"],
+                         lambda_redundancy=LAMBDA)
+    layer.reset_parameters(torch.Generator().manual_seed(seed + 1))
+    return layer.to(torch.bfloat16).to(dev)
+
+
+def _c3_input(cfg, seed, rank, pin):
+    g = torch.Generator().manual_seed(seed * 1000 + rank)
+    x = torch.randn(cfg["B"], cfg["N"], cfg["dim"], generator=g).to(torch.bfloat16)
+    return x.pin_memory() if pin else x
+
+
+def run_c3_ours(args, cfg, rank, world, local_rank):
+    """CABAttention forward (fused QKV projection, predictor, block-sparse
+    attention into the [B, N, dim] layout, output projection) on a device-resident x."""
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    from cab_attention import _lib
+    from cab_attention.kernels import block_sparse_attention
+    from cab_attention.kernels.sparse_attention import sparse_attention_flops
+    hbm, tf_burst, tf_sus, peak_kind = measured_peaks()
+    B, N, dim, H, D = cfg["B"], cfg["N"], cfg["dim"], cfg["Hq"], cfg["D"]
+    layer = _c3_layer(cfg, args.seed, dev)
+    x_h = _c3_input(cfg, args.seed, rank, pin=True)
+    x = x_h.to(dev)
+    out_h = torch.empty(B, N, dim, dtype=torch.bfloat16).pin_memory()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    def staged(ev):
+        ev[0].record()
+        qkv = layer.qkv(x)
+        q, k, v = layer.split_heads(qkv)
+        ev[1].record()
+        idx, num = layer.predictor.predict_blocks(q, k)
+        ev[2].record()
+        ctx = torch.empty(B, N, dim, dtype=x.dtype, device=dev)
+        block_sparse_attention(q, k, v, idx, num, BLOCK, out=ctx.view(B, N, H, D).transpose(1, 2))
+        ev[3].record()
+        out = layer.proj(ctx)
+        ev[4].record()
+        return out, num
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            layer(x)
+        torch.cuda.synchronize()
+        assert _lib.device_status() == 0
+        sampler = ClockSampler(local_rank)
+        sampler.start()
+        time.sleep(0.2)
+        barrier()
+        sampler.mark_start()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            layer(x)
+        end.record()
+        barrier()
+        sampler.mark_end()
+        clocks = sampler.stop()
+        t = torch.tensor([start.elapsed_time(end)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        step_ms = t.item() / args.steps
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+        for st in range(args.steps):
+            _, num = staged(evs[st])
+        torch.cuda.synchronize()
+        st_ms = [statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.steps))
+                 for j in range(4)]
+        # end to end through the module with host buffers: x in, out back, every step
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            out_h.copy_(layer(x_h.to(dev, non_blocking=True)), non_blocking=True)
+        e1.record()
+        barrier()
+        te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    attn_flop = sparse_attention_flops(num, BLOCK, D)
+    proj_flop = 2.0 * B * N * dim * 3 * dim
+    out_flop = 2.0 * B * N * dim * dim
+    achieved = attn_flop / st_ms[2] / 1e9
+    stages = {
+        "qkv_proj": {"ms": st_ms[0], "TFLOP/s": proj_flop / st_ms[0] / 1e9},
+        "predictor": {"ms": st_ms[1]},
+        "attention": {"ms": st_ms[2], "TFLOP/s": achieved, "frac_bf16": achieved / tf_sus,
+                      "kept_block_pairs": int(num.sum().item())},
+        "out_proj": {"ms": st_ms[3], "TFLOP/s": out_flop / st_ms[3] / 1e9},
+    }
+    if rank != 0:
+        return None
+    cpu = None
+    if world == 1 and args.cpu_baseline_seconds > 0:
+        ms, desc = c3_cpu_sample(cfg, args.cpu_baseline_seconds, args.seed)
+        cpu = {"value": ms, "unit": "ms", "cores": os.cpu_count(), "kind": "port", "sample": desc}
+    return {
+        "metric": "CABAttention layer ms @N=128k (dim 512, 8 heads)",
+        "value": step_ms / world, "unit": "ms", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (x iid N(0,1) bf16, seeded; weights N(0, 0.02^2) from the seed)",
+        "config": {"workload": cfg["workload"], "per_rank": f"B={B} N={N} dim={dim} heads={H} head_dim={D}",
+                   "parallelism": f"batch shards, {world} rank(s), no data-path collective",
+                   "l2": "x 262 MB and qkv 786 MB per rank > 126 MB L2; no flush needed"},
+        "stages": stages,
+        "roofline": {"bound": "tensor", "kernel": "attn_tc_kernel<64> (block-sparse attention, head_dim 64)",
+                     "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s", "frac": achieved / tf_sus,
+                     "peak_source": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a multi-ms step)",
+                     "traffic": None},
+        "cpu_baseline": cpu,
+        "e2e": {"value": te.item() / args.steps / world, "unit": "ms",
+                "h2d_bytes_per_step": world * x_h.numel() * 2, "d2h_bytes_per_step": world * out_h.numel() * 2},
+        # ours per forward: coarsen, two FRC GEMMs, top-k, pair-union, attention (the two
+        # projections are cuBLAS GEMMs)
+        "gpu_launches": 6 * args.steps,
+        "clocks": clocks,
+    }
+
+
+def c3_cpu_sample(cfg, seconds_budget, seed=0):
+    """Oracle sample of the layer: the predictor + attention sample of one head (cpu_sample
+    at head_dim 64) plus numpy fp32 projections of a row sample, extrapolated."""
+    import numpy as np
+    ms_pa, desc = cpu_sample(cfg, seconds_budget * 0.8, seed)
+    rows = 8192
+    g = np.random.default_rng(seed)
+    xs = g.standard_normal((rows, cfg["dim"]), dtype=np.float32)
+    w = g.standard_normal((4 * cfg["dim"], cfg["dim"]), dtype=np.float32) * 0.02
+    t0 = time.perf_counter()
+    xs @ w.T
+    dt = time.perf_counter() - t0
+    proj_ms = dt * 1e3 * cfg["B"] * cfg["N"] / rows
+    return ms_pa + proj_ms, desc + f"; projections: numpy fp32 GEMMs of {rows} rows ({dt:.2f} s), scaled to B*N rows"
 
 
 # --------------------------------------------------------------------------- predictor sweep
@@ -911,6 +1061,9 @@ def main():
                 res = run_flash_reference(args, cfg)
             elif args.config == "sweep":
                 res = run_sweep_reference(args, cfg)
+            elif args.config == "c3":
+                res = run_reference(args, cfg, sampler=c3_cpu_sample,
+                                    metric="CABAttention layer ms @N=128k (dim 512, 8 heads)")
             elif args.config in ("nodefrc", "evict"):
                 res = run_aux_reference(args, cfg)
             else:
@@ -924,7 +1077,7 @@ def main():
                                 device_id=torch.device("cuda", local_rank))
     try:
         run = {"flash": run_flash_ours, "nodefrc": run_aux_ours, "evict": run_aux_ours,
-               "sweep": run_sweep_ours}.get(args.config, run_ours)
+               "sweep": run_sweep_ours, "c3": run_c3_ours}.get(args.config, run_ours)
         res = run(args, cfg, rank, world, local_rank)
         if rank == 0 and res is not None:
             print(json.dumps(res), flush=True)
