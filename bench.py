@@ -410,7 +410,10 @@ def run_ours(args, cfg, rank, world, local_rank):
 # workload. "ns": the capture ran the north_star shape at 4 of its 16 (batch, head) units
 # (409.461 MB read + 116.139 MB written); DRAM traffic is per-unit (each unit reads its own
 # Q/K/V once and writes its own O), so the full launch is scaled by 16 / 4.
-ATTN_TRAFFIC_BYTES = {"ns": (409.461248e6 + 116.139264e6) * 4}
+ATTN_TRAFFIC_BYTES = {"ns": (409.461248e6 + 116.139264e6) * 4,
+                      # profiles/attn_tc_kernel_c3_headdim64.md: B=1 of the layer's B=2 (per-unit
+                      # traffic again), scaled by 2
+                      "c3": (500.599296e6 + 114.062592e6) * 2}
 
 
 # --------------------------------------------------------------------------- reference arm
@@ -567,7 +570,7 @@ def run_c3_ours(args, cfg, rank, world, local_rank):
         "roofline": {"bound": "tensor", "kernel": "attn_tc_kernel<64> (block-sparse attention, head_dim 64)",
                      "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s", "frac": achieved / tf_sus,
                      "peak_source": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a multi-ms step)",
-                     "traffic": None},
+                     "traffic": ATTN_TRAFFIC_BYTES.get("c3")},
         "cpu_baseline": cpu,
         "e2e": {"value": te.item() / args.steps / world, "unit": "ms",
                 "h2d_bytes_per_step": world * x_h.numel() * 2, "d2h_bytes_per_step": world * out_h.numel() * 2},
