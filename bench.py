@@ -21,7 +21,6 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -584,7 +583,6 @@ def run_c3_ours(args, cfg, rank, world, local_rank):
 def c3_cpu_sample(cfg, seconds_budget, seed=0):
     """Oracle sample of the layer: the predictor + attention sample of one head (cpu_sample
     at head_dim 64) plus numpy fp32 projections of a row sample, extrapolated."""
-    import numpy as np
     ms_pa, desc = cpu_sample(cfg, seconds_budget * 0.8, seed)
     rows = 8192
     g = np.random.default_rng(seed)
