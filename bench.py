@@ -655,9 +655,28 @@ def run_sweep_ours(args, cfg, rank, world, local_rank):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         st_ms = [statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.steps))
                  for j in range(3)]
+        # the same step captured in a CUDA graph: replays carry no per-call host work
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        graph.replay()
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        g1.record()
+        torch.cuda.synchronize()
+        graph_ms = g0.elapsed_time(g1) / args.steps
+        del graph
         M = (N + BLOCK - 1) // BLOCK
-        sweep[str(N)] = {"ms": t.item() / args.steps, "M": M, "k": kk, "coarsen_ms": st_ms[0],
-                         "frc_ms": st_ms[1], "topk_ms": st_ms[2]}
+        sweep[str(N)] = {"ms": t.item() / args.steps, "graph_ms": graph_ms, "M": M, "k": kk,
+                         "coarsen_ms": st_ms[0], "frc_ms": st_ms[1], "topk_ms": st_ms[2]}
         last = (N, M, kk, q_h, k_h, q, k, step, st_ms)
     clocks = sampler.stop()
 
