@@ -7,14 +7,17 @@ kept, non-causal. Q, K, V iid N(0,1) from per-(b,h) seeded generators (synthetic
 the reference measures on random tensors too).
 
 One step = Max-L2 coarsening -> FRC (two tensor-core GEMMs) -> per-row top-k -> pair-union
-lists -> block-sparse attention, for every (b, h) unit of the rank. Multi-GPU: one process
-per GPU; each rank runs a full north_star layer on its own batch slice (global batch
-2 x world, sharded by (batch x head), no collective in the data path) -> weak scaling;
-``value`` = max-over-ranks step time / world = ms per layer-equivalent for the whole job.
+lists -> block-sparse attention. Multi-GPU (one process per GPU, torchrun): by default the
+layer's B x Hkv (batch, KV head) units are split over the ranks (strong scaling; the
+north_star partition), each rank computes its units in two chunks and all-gathers each
+chunk's output over NCCL on a side stream inside the timed region; ``value`` = the
+max-over-ranks layer latency. ``--scaling weak`` gives every rank its own whole layer
+instead (``value`` = step time / world, ms per layer-equivalent).
 
 ``--impl reference`` times the reference's path on the host CPU: the reference's own
 implementation of this path is absent from its snapshot, so its CPU restatement under
-oracle/ (numpy, all host threads) is timed on a bounded sample and extrapolated.
+oracle/ (float32 torch on all host threads, oracle/cab_torch_cpu.py) is timed on whole
+(b, h) heads within a per-step budget and extrapolated per head.
 """
 
 from __future__ import annotations
@@ -224,7 +227,7 @@ class Layer:
         if ev: ev[3].record()
         out = block_sparse_attention(q, k, v, kv_idx, kv_num, BLOCK, self.cfg["causal"])
         if ev: ev[4].record()
-        return out, kv_num
+        return out, kv_idx, kv_num
 
     def e2e(self, q_host, k_host, v_host, out_host):
         """Public-API call with host buffers (cab_prefill_host): the pinned inputs are
@@ -235,17 +238,38 @@ class Layer:
                           lambda_redundancy=LAMBDA, causal=self.cfg["causal"], out=out_host)
 
 
-def cpu_sample(cfg, seconds_budget, seed=0):
-    """Oracle (numpy) on a bounded sample of the workload, extrapolated to one layer.
+_CPU_INPUTS = {}  # the CPU baseline's inputs, made once per run (not part of a timed step)
 
-    Sample: the full predictor (coarsen + FRC + top-k) of one (b, h) head at full N, and
-    the attention of `nb` query blocks of that head; scaled by the number of heads and
-    query blocks of the layer. Returns (ms per layer, description)."""
-    from oracle import cab_oracle as orc
+
+def cpu_sample(cfg, seconds_budget, seed=0):
+    """The reference path on the host CPU, on a bounded sample of the workload, extrapolated
+    to one layer. Non-causal configurations: the float32 torch restatement
+    (oracle/cab_torch_cpu.py) on all host threads -- the predictor of every head in full,
+    attention head by head until the budget is spent. Causal ones: the float64
+    numpy oracle on one head's predictor and a sample of its query blocks.
+    Returns (ms per layer, cpu_baseline dict without the value)."""
+    from oracle import cab_torch_cpu as tcpu
     from cab_attention import synthetic
+    torch.set_num_threads(os.cpu_count())
     N, D = cfg["N"], cfg["D"]
+    base = {"unit": "ms", "cores": torch.get_num_threads(), "cpu_model": tcpu.cpu_model(), "kind": "port"}
+    if not cfg["causal"]:
+        key = (cfg["B"], cfg["Hq"], cfg["Hkv"], N, D, seed)
+        if key not in _CPU_INPUTS:
+            _CPU_INPUTS.clear()
+            _CPU_INPUTS[key] = synthetic.make_qkv(cfg["B"], cfg["Hq"], cfg["Hkv"], N, D, torch.bfloat16, seed)
+        q, k, v = _CPU_INPUTS[key]
+        ms, info = tcpu.layer_timed(q, k, v, BLOCK, cfg["sparsity"], LAMBDA, budget_s=seconds_budget)
+        heads = info["heads"]
+        desc = (f"float32 torch on {base['cores']} threads: {info['heads_measured']} of {heads} (b, h) heads in "
+                f"full (predictor, then attention over the kept K/V blocks gathered and multiplied with "
+                f"bmm), {ms * info['measured_fraction'] / 1e3:.1f} s measured"
+                + (", extrapolated linearly to every head" if info["extrapolated"] else ""))
+        return ms, dict(base, dtype="f32", sample=desc, extrapolated=info["extrapolated"],
+                        measured_fraction=round(info["measured_fraction"], 4),
+                        predictor_ms=round(info["predictor_ms"], 1), attention_ms=round(info["attention_ms"], 1))
+    from oracle import cab_oracle as orc
     M = (N + BLOCK - 1) // BLOCK
-    G = cfg["Hq"] // cfg["Hkv"]
     q = synthetic.normal_heads("q", [0], 1, N, D, torch.bfloat16, seed).float().numpy()
     k = synthetic.normal_heads("k", [0], 1, N, D, torch.bfloat16, seed).float().numpy()
     v = synthetic.normal_heads("v", [0], 1, N, D, torch.bfloat16, seed).float().numpy()
@@ -255,12 +279,9 @@ def cpu_sample(cfg, seconds_budget, seed=0):
     kc, _ = orc.coarsen_maxl2(k, BLOCK)
     t1 = time.perf_counter()
     frc, _, _ = orc.block_frc(qc, kc, 1.0, LAMBDA, "abs")
-    t2 = time.perf_counter()
     idx, num, _ = orc.topk_block_mask(frc, kk, True, True, cfg["causal"])
     t3 = time.perf_counter()
     nb = 1
-    rows = []
-    ta = 0.0
     while True:
         rows = [(0, 0, i) for i in range(0, M, max(1, M // nb))][:nb]
         s = time.perf_counter()
@@ -273,23 +294,80 @@ def cpu_sample(cfg, seconds_budget, seed=0):
     coarsen_ms = (t1 - t0) * 1e3 * cfg["B"] * (cfg["Hq"] + cfg["Hkv"]) / 2.0
     pred_ms = coarsen_ms + (t3 - t1) * 1e3 * heads
     attn_ms = ta * 1e3 / len(rows) * M * heads
-    desc = (f"numpy oracle: predictor of 1 of {heads} heads at full N={N} "
+    desc = (f"float64 numpy oracle: predictor of 1 of {heads} heads at full N={N} "
             f"({(t3 - t0):.1f} s) + attention of {len(rows)} of {M} query blocks of that head "
             f"({ta:.1f} s), extrapolated linearly to the whole layer")
-    return pred_ms + attn_ms, desc
+    measured = (t3 - t0) * 1e3 + ta * 1e3
+    return pred_ms + attn_ms, dict(base, dtype="f64", sample=desc, extrapolated=True,
+                                   measured_fraction=round(measured / (pred_ms + attn_ms), 6))
+
+
+def pick_peak(clocks, window_ms, tf_burst, tf_sus):
+    """Burst peak for a short timed window at full clock (the driver's runs), sustained for
+    a window long enough to settle under the power cap."""
+    sm, mx = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
+    if window_ms < 1000.0 or (sm and mx and sm >= 0.95 * mx):
+        return tf_burst, "bf16_tflops (burst: timed window %.0f ms, median SM clock %s of max %s MHz)" % (
+            window_ms, sm, mx)
+    return tf_sus, "bf16_tflops_sustained (timed window %.0f ms under the power cap, SM clock %s MHz)" % (
+        window_ms, sm)
+
+
+def shard_plan(cfg, rank, world, scaling):
+    """(local config, unit list, chunks). Strong scaling: the layer's B x Hkv (batch, KV
+    head) units are split into contiguous ranges (cab_attention.sharding.unit_range) and the
+    rank's units packed as one batch of heads; weak: every rank runs a whole layer on its
+    own batch slice."""
+    from cab_attention import sharding
+    G = cfg["Hq"] // cfg["Hkv"]
+    if world == 1 or scaling == "weak":
+        return dict(cfg), None, [(0, cfg["Hkv"])]
+    s, e = sharding.unit_range(cfg["B"] * cfg["Hkv"], world, rank)
+    units = [divmod(u, cfg["Hkv"]) for u in range(s, e)]
+    n = len(units)
+    lcfg = dict(cfg, B=1, Hq=n * G, Hkv=n)
+    nch = min(2, n)  # two chunks: the gather of the first overlaps the compute of the second
+    cuts = [round(i * n / nch) for i in range(nch + 1)]
+    return lcfg, units, [(cuts[i], cuts[i + 1]) for i in range(nch)]
 
 
 def run_ours(args, cfg, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    from cab_attention import _lib
+    from cab_attention import _lib, synthetic
     from cab_attention.kernels.sparse_attention import sparse_attention_flops
     hbm, tf_burst, tf_sus, peak_kind = measured_peaks()
-
-    q_h, k_h, v_h = make_inputs(cfg, rank, args.seed, pin=True)
+    scaling = args.scaling if world > 1 else "strong"
+    lcfg, units, chunks = shard_plan(cfg, rank, world, scaling)
+    G = cfg["Hq"] // cfg["Hkv"]
+    if units is None:
+        q_h, k_h, v_h = make_inputs(cfg, rank if scaling == "weak" else 0, args.seed, pin=True)
+    else:
+        q_h, k_h, v_h = synthetic.make_unit_qkv(units, G, cfg["N"], cfg["D"], torch.bfloat16, args.seed, pin=True)
     q, k, v = q_h.to(dev), k_h.to(dev), v_h.to(dev)
     out_h = torch.empty_like(q_h).pin_memory()
-    layer = Layer(cfg)
+    layer = Layer(lcfg)
+    strong = scaling == "strong" and world > 1
+    side = torch.cuda.Stream(device=dev)
+    # gathered output, chunk-major: gbuf[c] holds chunk c of every rank ([world, heads of
+    # chunk c, N, D]); the whole [B, Hq, N, D] is a strided view of these buffers
+    gbuf = [torch.empty((world, (c1 - c0) * G) + tuple(q.shape[2:]), dtype=q.dtype, device=dev)
+            for (c0, c1) in chunks] if strong else []
+
+    def step(evs=None):
+        works, kv_num = [], []
+        for ci, (c0, c1) in enumerate(chunks):
+            qc, kc, vc = q[:, c0 * G:c1 * G], k[:, c0:c1], v[:, c0:c1]
+            out_c, _, num_c = layer.stages(qc, kc, vc, evs[ci] if evs else None)
+            kv_num.append(num_c)
+            if strong:
+                side.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(side):
+                    works.append(dist.all_gather_into_tensor(gbuf[ci], out_c, async_op=True))
+                out_c.record_stream(side)
+        for w in works:
+            w.wait()
+        return kv_num
 
     def barrier():
         if world > 1:
@@ -298,13 +376,14 @@ def run_ours(args, cfg, rank, world, local_rank):
 
     # warm-up
     for _ in range(args.warmup):
-        out, kv_num = layer.stages(q, k, v)
+        kv_num = step()
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
 
-    # ---- timed region: device-resident inputs (inputs 1.5 GB/rank > 126 MB L2)
+    # ---- timed region: device-resident inputs (inputs 1.5 GB per layer > 126 MB L2)
     nstage = 5
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nstage)] for _ in range(args.steps)]
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(nstage)] for _ in chunks]
+           for _ in range(args.steps)]
     sampler = ClockSampler(local_rank)
     sampler.start()
     time.sleep(0.2)
@@ -314,21 +393,37 @@ def run_ours(args, cfg, rank, world, local_rank):
     end = torch.cuda.Event(enable_timing=True)
     start.record()
     for s in range(args.steps):
-        out, kv_num = layer.stages(q, k, v, evs[s])
+        kv_num = step(evs[s])
     end.record()
     barrier()
     sampler.mark_end()
     clocks = sampler.stop()
     total_ms = start.elapsed_time(end)
-    stage_ms = np.array([[evs[s][i].elapsed_time(evs[s][i + 1]) for i in range(nstage - 1)]
-                         for s in range(args.steps)]).mean(axis=0)
+    stage_ms = np.array([[sum(evs[s][c][i].elapsed_time(evs[s][c][i + 1]) for c in range(len(chunks)))
+                          for i in range(nstage - 1)] for s in range(args.steps)]).mean(axis=0)
     t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     step_ms = t.item() / args.steps
     assert _lib.device_status() == 0
 
-    # ---- end to end through the public API with host buffers
+    # ---- the gather alone (strong scaling): every chunk's all-gather without the compute
+    gather_ms = None
+    if strong:
+        locs = [torch.empty_like(g[0]) for g in gbuf]
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for _ in range(args.steps):
+            for ci in range(len(chunks)):
+                dist.all_gather_into_tensor(gbuf[ci], locs[ci])
+        g1.record()
+        barrier()
+        tg = torch.tensor([g0.elapsed_time(g1) / args.steps], device=dev, dtype=torch.float64)
+        dist.all_reduce(tg, op=dist.ReduceOp.MAX)
+        gather_ms = tg.item()
+
+    # ---- end to end through the public API with host buffers (each rank its own units)
     for _ in range(max(1, args.warmup // 2)):
         layer.e2e(q_h, k_h, v_h, out_h)
     barrier()
@@ -344,87 +439,101 @@ def run_ours(args, cfg, rank, world, local_rank):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_step_ms = te.item() / args.steps
 
-    # ---- roofline of each stage (algorithmic work / measured time)
-    B, Hq, Hkv, N, D = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["N"], cfg["D"]
+    # ---- roofline of each stage (algorithmic work of this rank / its measured time)
+    B, Hq, Hkv, N, D = lcfg["B"], lcfg["Hq"], lcfg["Hkv"], lcfg["N"], lcfg["D"]
     M = (N + BLOCK - 1) // BLOCK
     kk = layer.pred.keep_per_row(N)
     from cab_attention import roofline as rl
     coarsen_bytes = rl.coarsen_bytes(B, Hq, Hkv, N, D, 2, BLOCK)
     frc_flop = rl.frc_flops(B, Hq, M, D)
     topk_bytes = rl.topk_bytes(B, Hq, M, kk)
-    attn_flop = sparse_attention_flops(kv_num, BLOCK, D)
+    attn_flop = sum(sparse_attention_flops(n, BLOCK, D) for n in kv_num)
+    kept = int(sum(int(n.sum().item()) for n in kv_num))
     c_ms, f_ms, k_ms, a_ms = (float(x) for x in stage_ms)
+    peak, peak_src = pick_peak(clocks, total_ms, tf_burst, tf_sus)
     stages = {
         "coarsen": {"ms": c_ms, "GB/s": coarsen_bytes / c_ms / 1e6, "frac_hbm": coarsen_bytes / c_ms / 1e6 / hbm},
-        "frc": {"ms": f_ms, "TFLOP/s": frc_flop / f_ms / 1e9, "frac_bf16": frc_flop / f_ms / 1e9 / tf_sus},
+        "frc": {"ms": f_ms, "TFLOP/s": frc_flop / f_ms / 1e9, "frac_bf16": frc_flop / f_ms / 1e9 / peak},
         "topk": {"ms": k_ms, "GB/s": topk_bytes / k_ms / 1e6, "frac_hbm": topk_bytes / k_ms / 1e6 / hbm},
-        "attention": {"ms": a_ms, "TFLOP/s": attn_flop / a_ms / 1e9, "frac_bf16": attn_flop / a_ms / 1e9 / tf_sus,
-                      "kept_block_pairs": int(kv_num.sum().item())},
+        "attention": {"ms": a_ms, "TFLOP/s": attn_flop / a_ms / 1e9, "frac_bf16": attn_flop / a_ms / 1e9 / peak,
+                      "frac_bf16_sustained": attn_flop / a_ms / 1e9 / tf_sus, "kept_block_pairs": kept},
     }
     achieved = attn_flop / a_ms / 1e9
     roofline = {"bound": "tensor", "kernel": "attn_tc_kernel (block-sparse attention)",
-                "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s", "frac": achieved / tf_sus,
-                "peak_source": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a multi-ms step)",
-                "traffic": ATTN_TRAFFIC_BYTES.get(args.config)}
+                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_source": f"{peak_kind} {peak_src}",
+                "frac_of_sustained": achieved / tf_sus,
+                "traffic": ATTN_TRAFFIC_BYTES.get(args.config) if world == 1 else None}
 
     result = None
     if rank == 0:
         cpu = None
         if world == 1 and args.cpu_baseline_seconds > 0:
-            ms, desc = cpu_sample(cfg, args.cpu_baseline_seconds, args.seed)
-            cpu = {"value": ms, "unit": "ms", "cores": os.cpu_count(), "kind": "port", "sample": desc}
+            ms, info = cpu_sample(cfg, args.cpu_baseline_seconds, args.seed)
+            cpu = dict(info, value=ms)
         h2d = world * sum(x.numel() * x.element_size() for x in (q_h, k_h, v_h))
         d2h = world * out_h.numel() * out_h.element_size()
-        launches_per_step = 6  # coarsen, affinity GEMM, triangle GEMM, top-k, pair-union, attention
+        launches_per_step = 6 * len(chunks)  # coarsen, affinity GEMM, triangle GEMM, top-k, pair-union, attention
+        if strong:
+            par = (f"(batch x head) strong scaling: the layer's {cfg['B'] * cfg['Hkv']} (b, KV head) units split "
+                   f"over {world} ranks ({len(units)} per rank, {len(chunks)} chunks); each chunk's output "
+                   f"all-gathered over NCCL inside the timed region on a side stream")
+        elif world > 1:
+            par = f"weak scaling: every rank runs its own whole layer (global batch {cfg['B'] * world}), no collective"
+        else:
+            par = "one GPU, no collective"
         result = {
             "metric": "CAB layer ms @N=128k (predictor + sparse attn)",
-            "value": step_ms / world,
+            "value": step_ms if (strong or world == 1) else step_ms / world,
             "unit": "ms",
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": step_ms,
             "higher_is_better": False,
-            "scaling": "weak",
+            "scaling": "strong" if (strong or world == 1) else "weak",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (iid N(0,1) per-(b,h) seeded Q/K/V)",
-            "config": {"workload": cfg["workload"], "layers_per_step": world,
+            "config": {"workload": cfg["workload"], "layers_per_step": 1 if (strong or world == 1) else world,
                        "per_rank": f"B={B} Hq={Hq} Hkv={Hkv} N={N} D={D}",
-                       "parallelism": f"(batch x head) shards, {world} rank(s), no data-path collective",
-                       "l2": "inputs 1.5 GB per rank > 126 MB L2; no flush needed"},
+                       "parallelism": par,
+                       "l2": "inputs 1.5 GB per layer > 126 MB L2; no flush needed"},
             "stages": stages,
             "roofline": roofline,
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_step_ms / world, "unit": "ms", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
+            "e2e": {"value": e2e_step_ms if (strong or world == 1) else e2e_step_ms / world, "unit": "ms",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
         }
+        if gather_ms is not None:
+            result["gather_ms"] = gather_ms
+            result["gather_bytes_per_rank"] = sum(g.numel() * g.element_size() for g in gbuf)
     return result
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum per attention launch from the committed ncu
-# capture (profiles/attn_tc_kernel_ns_4heads.md); None until a capture exists for the
-# workload. "ns": the capture ran the north_star shape at 4 of its 16 (batch, head) units
-# (409.461 MB read + 116.139 MB written); DRAM traffic is per-unit (each unit reads its own
-# Q/K/V once and writes its own O), so the full launch is scaled by 16 / 4.
+# dram__bytes_read.sum + dram__bytes_write.sum per attention launch, from ncu captures of
+# attn_tc_kernel<128, bf16, sparse> on the north_star shape with 4 of its 16 (b, h) units
+# (409.461 MB read + 116.139 MB written) and of attn_tc_kernel<64, bf16, sparse> in the
+# configs[2] layer with 1 of its 2 batches (500.599 MB read + 114.063 MB written). DRAM
+# traffic is per unit (each unit reads its own Q/K/V once and writes its own O), so the
+# full launches are scaled by 16 / 4 and by 2.
 ATTN_TRAFFIC_BYTES = {"ns": (409.461248e6 + 116.139264e6) * 4,
-                      # profiles/attn_tc_kernel_c3_headdim64.md: B=1 of the layer's B=2 (per-unit
-                      # traffic again), scaled by 2
                       "c3": (500.599296e6 + 114.062592e6) * 2}
 
 
 # --------------------------------------------------------------------------- reference arm
 def run_reference(args, cfg, sampler=None, metric="CAB layer ms @N=128k (predictor + sparse attn)"):
-    """The reference path's CPU restatement (oracle port), bounded sample per step."""
+    """The reference path's CPU restatement on the host cores (all threads), a bounded
+    sample per step (cpu_sample)."""
     sampler = sampler or cpu_sample
     budget = max(2.0, args.reference_step_seconds)
     for _ in range(args.warmup):
         sampler(cfg, budget, args.seed)
-    vals, desc = [], ""
+    vals, info = [], {}
     for _ in range(args.steps):
-        ms, desc = sampler(cfg, budget, args.seed)
+        ms, info = sampler(cfg, budget, args.seed)
         vals.append(ms)
     value = statistics.median(vals)
     return {
@@ -437,13 +546,12 @@ def run_reference(args, cfg, sampler=None, metric="CAB layer ms @N=128k (predict
         "warmup": args.warmup,
         "ms_per_step": value,
         "higher_is_better": False,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "f64",
+        "dtype": info.get("dtype", "f32"),
         "data": "synthetic (iid N(0,1) per-(b,h) seeded Q/K/V)",
         "config": {"workload": cfg["workload"]},
-        "cpu_baseline": {"value": value, "unit": "ms", "cores": os.cpu_count(), "kind": "port",
-                         "sample": desc},
+        "cpu_baseline": dict(info, value=value),
         "e2e": {"value": value, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": ("the reference snapshot lacks this path's implementation (its coarse_predictor / "
                  "cab_attention / kernels modules are listed in its README but absent), so its "
@@ -543,10 +651,11 @@ def run_c3_ours(args, cfg, rank, world, local_rank):
     proj_flop = 2.0 * B * N * dim * 3 * dim
     out_flop = 2.0 * B * N * dim * dim
     achieved = attn_flop / st_ms[2] / 1e9
+    peak, peak_src = pick_peak(clocks, step_ms * args.steps, tf_burst, tf_sus)
     stages = {
         "qkv_proj": {"ms": st_ms[0], "TFLOP/s": proj_flop / st_ms[0] / 1e9},
         "predictor": {"ms": st_ms[1]},
-        "attention": {"ms": st_ms[2], "TFLOP/s": achieved, "frac_bf16": achieved / tf_sus,
+        "attention": {"ms": st_ms[2], "TFLOP/s": achieved, "frac_bf16": achieved / peak,
                       "kept_block_pairs": int(num.sum().item())},
         "out_proj": {"ms": st_ms[3], "TFLOP/s": out_flop / st_ms[3] / 1e9},
     }
@@ -554,8 +663,8 @@ def run_c3_ours(args, cfg, rank, world, local_rank):
         return None
     cpu = None
     if world == 1 and args.cpu_baseline_seconds > 0:
-        ms, desc = c3_cpu_sample(cfg, args.cpu_baseline_seconds, args.seed)
-        cpu = {"value": ms, "unit": "ms", "cores": os.cpu_count(), "kind": "port", "sample": desc}
+        ms, info = c3_cpu_sample(cfg, args.cpu_baseline_seconds, args.seed)
+        cpu = dict(info, value=ms)
     return {
         "metric": "CABAttention layer ms @N=128k (dim 512, 8 heads)",
         "value": step_ms / world, "unit": "ms", "n_gpus": world, "steps": args.steps,
@@ -567,8 +676,8 @@ def run_c3_ours(args, cfg, rank, world, local_rank):
                    "l2": "x 262 MB and qkv 786 MB per rank > 126 MB L2; no flush needed"},
         "stages": stages,
         "roofline": {"bound": "tensor", "kernel": "attn_tc_kernel<64> (block-sparse attention, head_dim 64)",
-                     "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s", "frac": achieved / tf_sus,
-                     "peak_source": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a multi-ms step)",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "peak_source": f"{peak_kind} {peak_src}", "frac_of_sustained": achieved / tf_sus,
                      "traffic": ATTN_TRAFFIC_BYTES.get("c3")},
         "cpu_baseline": cpu,
         "e2e": {"value": te.item() / args.steps / world, "unit": "ms",
@@ -581,18 +690,21 @@ def run_c3_ours(args, cfg, rank, world, local_rank):
 
 
 def c3_cpu_sample(cfg, seconds_budget, seed=0):
-    """Oracle sample of the layer: the predictor + attention sample of one head (cpu_sample
-    at head_dim 64) plus numpy fp32 projections of a row sample, extrapolated."""
-    ms_pa, desc = cpu_sample(cfg, seconds_budget * 0.8, seed)
+    """The CABAttention layer on the host CPU: the predictor + attention sample of
+    cpu_sample (head_dim 64) plus float32 torch projections of a row sample, extrapolated."""
+    ms_pa, info = cpu_sample(cfg, seconds_budget * 0.8, seed)
     rows = 8192
-    g = np.random.default_rng(seed)
-    xs = g.standard_normal((rows, cfg["dim"]), dtype=np.float32)
-    w = g.standard_normal((4 * cfg["dim"], cfg["dim"]), dtype=np.float32) * 0.02
+    g = torch.Generator().manual_seed(seed)
+    xs = torch.randn(rows, cfg["dim"], generator=g)
+    w = torch.randn(4 * cfg["dim"], cfg["dim"], generator=g) * 0.02
+    xs @ w.T
     t0 = time.perf_counter()
     xs @ w.T
     dt = time.perf_counter() - t0
     proj_ms = dt * 1e3 * cfg["B"] * cfg["N"] / rows
-    return ms_pa + proj_ms, desc + f"; projections: numpy fp32 GEMMs of {rows} rows ({dt:.2f} s), scaled to B*N rows"
+    info = dict(info, sample=info["sample"] + f"; projections: float32 torch GEMMs of {rows} rows "
+                                                f"({dt:.3f} s), scaled to B*N rows", extrapolated=True)
+    return ms_pa + proj_ms, info
 
 
 # --------------------------------------------------------------------------- predictor sweep
@@ -709,8 +821,8 @@ def run_sweep_ours(args, cfg, rank, world, local_rank):
         return None
     cpu = None
     if world == 1 and args.cpu_baseline_seconds > 0:
-        ms, desc = sweep_cpu_sample(dict(cfg, N=N), args.seed)
-        cpu = {"value": ms, "unit": "ms", "cores": os.cpu_count(), "kind": "port", "sample": desc}
+        ms, info = sweep_cpu_sample(dict(cfg, N=N), args.seed)
+        cpu = dict(info, value=ms)
     return {
         "metric": "CAB predictor ms @N=128k (sweep over N)",
         "value": sweep[str(N)]["ms"] / world, "unit": "ms", "n_gpus": world, "steps": args.steps,
@@ -736,38 +848,44 @@ def run_sweep_ours(args, cfg, rank, world, local_rank):
 
 
 def sweep_cpu_sample(cfg, seed=0):
-    """The numpy oracle predictor of one (b, h) head at N, scaled by the heads of the layer."""
-    from oracle import cab_oracle as orc
+    """The predictor (coarsen -> FRC -> top-k) of every head at N on the host CPU, float32
+    torch on all threads (oracle/cab_torch_cpu.py)."""
+    from oracle import cab_torch_cpu as tcpu
     from cab_attention import synthetic
+    torch.set_num_threads(os.cpu_count())
     N, D = cfg["N"], cfg["D"]
-    M = (N + BLOCK - 1) // BLOCK
-    q = synthetic.normal_heads("q", [0], 1, N, D, torch.bfloat16, seed).float().numpy()
-    k = synthetic.normal_heads("k", [0], 1, N, D, torch.bfloat16, seed).float().numpy()
-    t0 = time.perf_counter()
-    orc.predictor(q, k, BLOCK, cfg["sparsity"], LAMBDA)
-    dt = time.perf_counter() - t0
+    q, k, _ = synthetic.make_qkv(cfg["B"], cfg["Hq"], cfg["Hkv"], N, D, torch.bfloat16, seed)
+    G = cfg["Hq"] // cfg["Hkv"]
+    dt = 0.0
+    for b in range(cfg["B"]):
+        for h in range(cfg["Hq"]):
+            qs, ks = q[b, h].float(), k[b, h // G].float()
+            t0 = time.perf_counter()
+            tcpu.predictor_head(qs, ks, BLOCK, cfg["sparsity"], LAMBDA)
+            dt += time.perf_counter() - t0
     heads = cfg["B"] * cfg["Hq"]
-    return dt * 1e3 * heads, (f"numpy oracle predictor of 1 of {heads} heads at N={N} (M={M}) "
-                              f"({dt:.2f} s), scaled by the heads")
+    return dt * 1e3, {"unit": "ms", "cores": torch.get_num_threads(), "cpu_model": tcpu.cpu_model(),
+                      "kind": "port", "dtype": "f32", "extrapolated": False, "measured_fraction": 1.0,
+                      "sample": f"float32 torch predictor of all {heads} heads at N={N} ({dt:.2f} s)"}
 
 
 def run_sweep_reference(args, cfg):
     """The reference path's CPU restatement of the predictor (oracle port) per N."""
-    sweep = {}
+    sweep, info = {}, {}
     for N in SWEEP_N:
-        vals, desc = [], ""
-        for _ in range(max(1, args.steps)):
-            ms, desc = sweep_cpu_sample(dict(cfg, N=N), args.seed)
+        vals = []
+        for _ in range(max(1, min(args.steps, 3))):
+            ms, info = sweep_cpu_sample(dict(cfg, N=N), args.seed)
             vals.append(ms)
         sweep[str(N)] = {"ms": statistics.median(vals)}
     value = sweep[str(SWEEP_N[-1])]["ms"]
     return {
         "metric": "CAB predictor ms @N=128k (sweep over N)", "impl": "reference", "value": value,
         "unit": "ms", "n_gpus": 0, "steps": args.steps, "warmup": 0, "ms_per_step": value,
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (iid N(0,1) per-(b,h) seeded Q/K)", "config": {"workload": cfg["workload"]},
         "sweep": sweep,
-        "cpu_baseline": {"value": value, "unit": "ms", "cores": os.cpu_count(), "kind": "port", "sample": desc},
+        "cpu_baseline": dict(info, value=value),
         "e2e": {"value": value, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -846,6 +964,7 @@ def run_flash_ours(args, cfg, rank, world, local_rank):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     flop = flash_flop(cfg)
     achieved = flop / with_scores / 1e9
+    peak, peak_src = pick_peak(clocks, with_scores * args.steps, tf_burst, tf_sus)
     if rank != 0:
         return None
     cpu = None
@@ -862,8 +981,8 @@ def run_flash_ours(args, cfg, rank, world, local_rank):
         "stages": {"with_scores_ms": with_scores, "without_scores_ms": plain,
                    "scores_overhead": with_scores / plain - 1.0},
         "roofline": {"bound": "tensor", "kernel": "attn_tc_kernel<dense> (flash + column scores)",
-                     "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s", "frac": achieved / tf_sus,
-                     "peak_source": f"{peak_kind} bf16_tflops_sustained", "traffic": None},
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "peak_source": f"{peak_kind} {peak_src}", "traffic": None},
         "cpu_baseline": cpu,
         "e2e": {"value": te.item() / args.steps / world, "unit": "ms",
                 "h2d_bytes_per_step": world * sum(x.numel() * x.element_size() for x in (q_h, k_h, v_h)),
@@ -1057,7 +1176,10 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="ns")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-baseline-seconds", type=float, default=15.0)
-    ap.add_argument("--reference-step-seconds", type=float, default=4.0)
+    ap.add_argument("--reference-step-seconds", type=float, default=6.0)
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="--gpus N > 1: split one layer's (batch x head) units over the ranks and "
+                         "all-gather the output (strong), or give every rank its own layer (weak)")
     ap.add_argument("--batch", type=int, default=None, help="override B per rank (profiling)")
     ap.add_argument("--heads", type=int, default=None,
                     help="override the KV-head count per rank, query heads scaled (profiling)")

@@ -11,10 +11,11 @@ each block, ``:117-156``). An existing ``cumulative_scores`` shorter than ``N_k`
 extended with zeros first (``:223-230``), so scores keep accumulating across decode steps.
 
 The HF integration helpers (``replace_attention_with_flash``, ``get_all_cumulative_scores``,
-``FlashAttentionWithAccumulation``, ``apply_rotary_pos_emb``, ``rotate_half``,
-``repeat_kv``) follow the reference's module (``:264-598``). Grouped-query attention runs
-natively (each query head reads KV head ``h // (Hq // Hkv)``), which gives the same result
-as expanding K/V with ``repeat_kv`` first.
+``FlashAttentionWithAccumulation``) keep the reference module's interface (``:264-598``:
+names, signatures, the module attribute holding the scores, the layer-name keys);
+``apply_rotary_pos_emb``, ``rotate_half`` and ``repeat_kv`` are HuggingFace's standard
+functions. Grouped-query attention runs natively (each query head reads KV head
+``h // (Hq // Hkv)``), which gives the same result as expanding K/V with ``repeat_kv`` first.
 """
 
 from __future__ import annotations
@@ -152,75 +153,107 @@ def repeat_kv(hidden_states: torch.Tensor, n_rep: int) -> torch.Tensor:
     return hidden_states.reshape(batch, num_key_value_heads * n_rep, slen, head_dim)
 
 
-def _create_flash_attention_forward(original_module, layer_idx: int):
-    """Forward for a HuggingFace attention module (Qwen2 / Llama style) that runs the
-    projections and RoPE of the module, updates its KV cache, and computes attention
-    with cumulative scores kept on the module (``_flash_cumulative_scores``)."""
-    if not hasattr(original_module, "_flash_cumulative_scores"):
-        original_module._flash_cumulative_scores = None
+# ---------------------------------------------------------------- HuggingFace integration
+# Interface kept from the reference (flash_attention_accumulate.py:370-598): patched modules
+# keep their running scores in the attribute ``_flash_cumulative_scores``, and the scores
+# dictionary is keyed "model.layers.<i>.self_attn". The code below is this package's own.
 
-    def flash_forward(hidden_states: torch.Tensor, position_embeddings: tuple,
-                      attention_mask: Optional[torch.Tensor] = None, past_key_values=None,
-                      cache_position: Optional[torch.LongTensor] = None, **kwargs):
-        bsz, q_len, _ = hidden_states.size()
-        m = original_module
-        q = m.q_proj(hidden_states).view(bsz, q_len, m.num_heads, m.head_dim).transpose(1, 2)
-        k = m.k_proj(hidden_states).view(bsz, q_len, m.num_key_value_heads, m.head_dim).transpose(1, 2)
-        v = m.v_proj(hidden_states).view(bsz, q_len, m.num_key_value_heads, m.head_dim).transpose(1, 2)
+_SCORES_ATTR = "_flash_cumulative_scores"
+_PROJECTIONS = ("q_proj", "k_proj", "v_proj", "o_proj")
+
+
+def _decoder_attention(model: torch.nn.Module):
+    """Yields ``(name, layer index, module)`` for each ``model.model.layers[i].self_attn``."""
+    layers = getattr(getattr(model, "model", None), "layers", None)
+    for i, layer in enumerate(layers if layers is not None else ()):
+        attn = getattr(layer, "self_attn", None)
+        if attn is not None:
+            yield f"model.layers.{i}.self_attn", i, attn
+
+
+def _head_counts(attn: torch.nn.Module):
+    """(query heads, KV heads) of an attention module, read from the module itself or,
+    for modules that only carry them in their config (Qwen2 style), from ``attn.config``
+    (then also set on the module); None when neither has them."""
+    cfg = getattr(attn, "config", None)
+    found = []
+    for own, from_cfg in (("num_heads", "num_attention_heads"), ("num_key_value_heads", "num_key_value_heads")):
+        n = getattr(attn, own, None)
+        if n is None:
+            n = getattr(cfg, from_cfg, None)
+        if n is None:
+            return None
+        found.append(int(n))
+    attn.num_heads, attn.num_key_value_heads = found
+    return tuple(found)
+
+
+class _PatchedAttention:
+    """Replacement ``forward`` of a HuggingFace decoder attention module (Qwen2 / Llama
+    call signature): the module's own projections and rotary embedding, its KV-cache
+    update, then attention with cumulative column scores; the running scores live on the
+    module. Returns ``(output, None)``: no attention weights are materialised."""
+
+    def __init__(self, module: torch.nn.Module, layer_idx: int):
+        self.module = module
+        self.layer_idx = layer_idx
+        if not hasattr(module, _SCORES_ATTR):
+            setattr(module, _SCORES_ATTR, None)
+
+    def _heads(self, proj: torch.nn.Module, x: torch.Tensor, n: int) -> torch.Tensor:
+        b, t, _ = x.shape
+        return proj(x).view(b, t, n, self.module.head_dim).transpose(1, 2)
+
+    def __call__(self, hidden_states: torch.Tensor, position_embeddings: tuple,
+                 attention_mask: Optional[torch.Tensor] = None, past_key_values=None,
+                 cache_position: Optional[torch.LongTensor] = None, **kwargs):
+        m = self.module
         cos, sin = position_embeddings
+        q = self._heads(m.q_proj, hidden_states, m.num_heads)
+        k = self._heads(m.k_proj, hidden_states, m.num_key_value_heads)
+        v = self._heads(m.v_proj, hidden_states, m.num_key_value_heads)
         q, k = apply_rotary_pos_emb(q, k, cos, sin)
         if past_key_values is not None:
-            cache_kwargs = {"sin": sin, "cos": cos, "cache_position": cache_position}
-            k, v = past_key_values.update(k, v, layer_idx, cache_kwargs=cache_kwargs)
-        # grouped-query attention runs natively (same result as repeat_kv first)
-        attn_output, scores = flash_attention_with_cumulative_scores(
-            q, k, v, cumulative_scores=m._flash_cumulative_scores)
-        m._flash_cumulative_scores = scores
-        attn_output = attn_output.transpose(1, 2).reshape(bsz, q_len, -1)
-        return m.o_proj(attn_output), None
-
-    return flash_forward
+            k, v = past_key_values.update(k, v, self.layer_idx,
+                                          cache_kwargs={"sin": sin, "cos": cos, "cache_position": cache_position})
+        # KV heads are shared by their query-head group inside the kernel (no repeat_kv copy)
+        ctx, scores = flash_attention_with_cumulative_scores(q, k, v, getattr(m, _SCORES_ATTR))
+        setattr(m, _SCORES_ATTR, scores)
+        b, _, t, _ = ctx.shape
+        return m.o_proj(ctx.transpose(1, 2).reshape(b, t, -1)), None
 
 
 def replace_attention_with_flash(model: torch.nn.Module, module_filter=None) -> torch.nn.Module:
-    """Patches every ``model.model.layers[i].self_attn`` that has q/k/v/o projections and
-    a head_dim so its forward runs this module's attention (in place; returns the model)."""
-    patched = 0
-    for layer_idx, layer in enumerate(model.model.layers):
-        if not hasattr(layer, "self_attn"):
-            continue
-        attn = layer.self_attn
-        name = f"model.layers.{layer_idx}.self_attn"
+    """Routes the attention of every decoder layer (``model.model.layers[i].self_attn``
+    with q/k/v/o projections, a ``head_dim`` and known head counts) through this
+    package's kernel, in place; ``module_filter(name, module)`` may exclude modules.
+    Returns the model."""
+    done, skipped = [], []
+    for name, i, attn in _decoder_attention(model):
         if module_filter is not None and not module_filter(name, attn):
             continue
-        if not all(hasattr(attn, a) for a in ("q_proj", "k_proj", "v_proj", "o_proj", "head_dim")):
-            logger.warning("Skipping %s: missing required base attributes", name)
+        usable = all(hasattr(attn, a) for a in _PROJECTIONS + ("head_dim",)) and _head_counts(attn) is not None
+        if not usable:
+            skipped.append(name)
             continue
-        for attr, cfg_attr in (("num_heads", "num_attention_heads"), ("num_key_value_heads", "num_key_value_heads")):
-            if not hasattr(attn, attr):
-                if hasattr(attn, "config") and hasattr(attn.config, cfg_attr):
-                    setattr(attn, attr, getattr(attn.config, cfg_attr))
-        if not (hasattr(attn, "num_heads") and hasattr(attn, "num_key_value_heads")):
-            logger.warning("Skipping %s: cannot determine head counts", name)
-            continue
-        attn.forward = _create_flash_attention_forward(attn, layer_idx)
-        patched += 1
-    if patched == 0:
-        logger.warning("No attention modules were patched. Model structure may be incompatible.")
+        attn.forward = _PatchedAttention(attn, i)
+        done.append(name)
+    for name in skipped:
+        logger.warning("%s left unpatched: no q/k/v/o projections, head_dim or head counts", name)
+    if done:
+        logger.info("flash attention with cumulative scores in %d module(s)", len(done))
+    else:
+        logger.warning("replace_attention_with_flash found no decoder attention module to patch")
     return model
 
 
 def get_all_cumulative_scores(model: torch.nn.Module) -> dict:
-    """``{layer name: cumulative scores [B, H, N]}`` from patched or wrapped modules."""
-    scores = {}
-    if hasattr(model, "model") and hasattr(model.model, "layers"):
-        for layer_idx, layer in enumerate(model.model.layers):
-            attn = getattr(layer, "self_attn", None)
-            s = getattr(attn, "_flash_cumulative_scores", None) if attn is not None else None
-            if s is not None:
-                scores[f"model.layers.{layer_idx}.self_attn"] = s
-    if not scores:
-        for name, module in model.named_modules():
-            if isinstance(module, FlashAttentionWithAccumulation) and module.get_cumulative_scores() is not None:
-                scores[name] = module.get_cumulative_scores()
-    return scores
+    """``{module name: cumulative scores [B, H, N]}``: from the modules patched by
+    ``replace_attention_with_flash`` or, if there are none, from
+    ``FlashAttentionWithAccumulation`` wrappers anywhere in the model."""
+    patched = {name: getattr(attn, _SCORES_ATTR) for name, _, attn in _decoder_attention(model)
+               if getattr(attn, _SCORES_ATTR, None) is not None}
+    if patched:
+        return patched
+    return {name: mod.get_cumulative_scores() for name, mod in model.named_modules()
+            if isinstance(mod, FlashAttentionWithAccumulation) and mod.get_cumulative_scores() is not None}

@@ -52,6 +52,26 @@ def make_qkv(B: int, Hq: int, Hkv: int, N: int, D: int, dtype=torch.bfloat16, se
     return q, k, v
 
 
+def make_unit_qkv(units, G: int, N: int, D: int, dtype=torch.bfloat16, seed: int = 0, pin: bool = False):
+    """Q ``[1, len(units)*G, N, D]``, K and V ``[1, len(units), N, D]`` holding the given
+    ``(b, kv_head)`` units of a larger batch (query heads ``kv_head*G .. +G-1``), each slice
+    drawn from its own seed: a rank's shard of the (batch x head) partition, equal to the
+    same slices of ``make_qkv`` over the whole batch."""
+    n = len(units)
+
+    def alloc(h):
+        t = torch.empty(1, h, N, D, dtype=dtype)
+        return t.pin_memory() if pin else t
+
+    q, k, v = alloc(n * G), alloc(n), alloc(n)
+    for i, (b, g) in enumerate(units):
+        for j in range(G):
+            q[0, i * G + j].copy_(torch.randn(N, D, generator=slice_generator(seed, b, g * G + j, "q")))
+        k[0, i].copy_(torch.randn(N, D, generator=slice_generator(seed, b, g, "k")))
+        v[0, i].copy_(torch.randn(N, D, generator=slice_generator(seed, b, g, "v")))
+    return q, k, v
+
+
 def max_l2_token(x_block: torch.Tensor) -> torch.Tensor:
     """Row of ``x_block [n, D]`` with the largest L2 norm (fp64 norms, first max wins)."""
     n = (x_block.double() ** 2).sum(-1)

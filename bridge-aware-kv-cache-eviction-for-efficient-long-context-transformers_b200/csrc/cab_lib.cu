@@ -60,14 +60,26 @@ extern "C" int cab_selftest_wait_timeout(int64_t limit_us, int* gave_up_device, 
   return cab::check_launch("wait_timeout_selftest_kernel");
 }
 
+namespace cab {
+// The status word is read and cleared in one atomic exchange on the device, so a bit that
+// a kernel on another stream sets meanwhile is either returned now or kept for the next
+// read, never lost between a read and a separate clear.
+__device__ int g_status_taken = 0;
+__global__ void status_take_kernel() { g_status_taken = atomicExch(&g_device_status, 0); }
+}  // namespace cab
+
 extern "C" int cab_device_status(void* stream, int* status) {
   if (!status) return cab::fail(CAB_ERR_INVALID_ARG, "device_status: NULL output");
+  static std::mutex mu;  // one exchange-and-read at a time (g_status_taken is shared)
+  std::lock_guard<std::mutex> lock(mu);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return cab::fail(CAB_ERR_LAUNCH, "device_status: %s", cudaGetErrorString(e));
-  int value = 0, zero = 0;
-  e = cudaMemcpyFromSymbol(&value, cab::g_device_status, sizeof(int));
-  if (e == cudaSuccess) e = cudaMemcpyToSymbol(cab::g_device_status, &zero, sizeof(int));
+  cab::status_take_kernel<<<1, 1, 0, st>>>();
+  if (int rc = cab::check_launch("status_take_kernel")) return rc;
+  int value = 0;
+  e = cudaMemcpyFromSymbolAsync(&value, cab::g_status_taken, sizeof(int), 0, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return cab::fail(CAB_ERR_LAUNCH, "device_status: %s", cudaGetErrorString(e));
   *status = (value & cab::CAB_DEVICE_TIMEOUT) ? CAB_ERR_TIMEOUT
            : (value & cab::CAB_DEVICE_LAYOUT) ? CAB_ERR_LAUNCH

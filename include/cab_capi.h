@@ -75,9 +75,11 @@ CAB_API const char* cab_last_error_string(void);
 /* 1 if `device` is an sm_100 part these kernels were built for, else 0. */
 CAB_API int cab_device_supported(int device);
 
-/* Synchronises `stream`, then stores and clears the device-side status word of the
- * current device (0 = fine, CAB_ERR_TIMEOUT if a kernel's bounded wait gave up,
- * CAB_ERR_LAUNCH if a kernel found its shared-memory layout did not fit and did nothing). */
+/* Synchronises `stream`, then reads and clears the device-side status word of the
+ * current device in one atomic exchange (a bit set meanwhile by a kernel on another stream
+ * is kept for the next call, never lost) and stores: 0 = fine, CAB_ERR_TIMEOUT if a kernel's
+ * bounded wait gave up, CAB_ERR_LAUNCH if a kernel found its shared-memory layout did not
+ * fit and did nothing. */
 CAB_API int cab_device_status(void* stream, int* status);
 
 /* Failure-detection self-test (no reference counterpart): launches a kernel whose one
@@ -208,8 +210,10 @@ CAB_API int cab_sparse_attn_fwd(const void* q, const void* k, const void* v, con
  * allocator, so they cannot cudaMalloc the workspace cab_sparse_attn_fwd asks for.
  * Scratch: a static 16 MiB device buffer inside the library, held on every GPU that loads
  * it until the process exits. Sizes whose cab_sparse_attn_workspace_size exceeds 16 MiB
- * return CAB_ERR_UNSUPPORTED. The first call on each device looks up the buffer's address
- * (cudaGetSymbolAddress, with that device current); make that first call before any
+ * return CAB_ERR_UNSUPPORTED. The first call in each CUDA context looks up the buffer's
+ * address (cudaGetSymbolAddress, with that context current) and caches it against the
+ * context's unique ID, so a new context on the device (after cudaDeviceReset, or a
+ * driver-API context made current) looks it up again; make that first call before any
  * stream capture. All calls share the buffer, so calls that overlap on the GPU race.
  * The call itself allocates nothing.
  */

@@ -1,11 +1,15 @@
-"""Full-size configurations through the public API: configs[1] (C2: B2 H8 N32768 D128 bf16,
+"""Full-size configurations through the public API: the north_star layer itself (B2 H8
+N128000 D128 bf16, s=0.95, k=100; the workload bench.py times, through the bench step's own
+calls), configs[1] (C2: B2 H8 N32768 D128 bf16,
 s=0.95, one planted bridge per (b, h)), configs[2] (C3: the CABAttention layer, dim 512,
 8 heads of 64, B2 N128000 bf16, s=0.95, projection weights N(0, 0.02^2)), configs[3] (C4:
 the predictor over N in {1k, 4k, 16k, 64k, 128k}, B2 H8 D128 bf16, s=0.95) and configs[4]
 (C5: GQA 32/8, B1 N65536 D128 bf16, causal, s=0.99, four planted bridges). Checked by
 size-independent properties: every planted bridge is kept; on sampled heads the block
-mask agrees with the float64 oracle (>= 99.9 % of all blocks, >= 99 % of kept blocks: fp16
-triangle products move a few near-tied blocks); attention on sampled query blocks
+mask agrees with the float64 oracle (>= 99.9 % of all blocks; of kept blocks >= 99.9 % for
+the north_star layer, C2 and C5, where 99.945-99.99 % was measured, and >= 99 % for C3 and
+the C4 sweep, whose small-M cases keep few blocks per row: fp16 triangle products move a
+few near-tied blocks); attention on sampled query blocks
 matches the oracle given the same lists (max abs error <= 2e-2); the layer output on
 sampled rows matches the output projection of the oracle attention (max abs error
 <= 2e-3 at these weight scales)."""
@@ -48,7 +52,7 @@ def test_full_size_config(name):
         want = o["mask"][0, 0]
         got = d[b, h]
         assert (got == want).mean() >= 0.999
-        assert (got & want).sum() / want.sum() >= 0.99
+        assert (got & want).sum() / want.sum() >= 0.999
         M = c["M"]
         rows = [(0, 0, i) for i in (0, 1, M // 3, M // 2 + 1, M - 2, M - 1)]
         att, _ = orc.block_sparse_attention(qs, ks, vs, idx_h[b:b + 1, h:h + 1], num_h[b:b + 1, h:h + 1], 64,
@@ -60,9 +64,52 @@ def test_full_size_config(name):
             assert err <= 2e-2, (b, h, i, err)
 
 
-def _mask_agrees(got, want):
+def _lists_to_dense(idx, num, M):
+    got = np.zeros((M, M), dtype=bool)
+    for i in range(M):
+        got[i, idx[i, :num[i]]] = True
+    return got
+
+
+def test_north_star_layer():
+    """The benchmarked workload, with the exact stage calls of bench.Layer.stages: coarsen
+    -> FRC -> top-k (k = 100 of M = 2000) -> block-sparse attention. On two sampled heads
+    the block mask agrees with the float64 oracle on >= 99.9 % of all blocks and of kept
+    blocks, and attention on six sampled query blocks per head matches the oracle given the
+    same lists (max abs error <= 2e-2)."""
+    import bench
+    cfg = bench.CONFIGS["ns"]
+    q_h, k_h, v_h = bench.make_inputs(cfg, 0, 0, pin=False)
+    q, k, v = q_h.cuda(), k_h.cuda(), v_h.cuda()
+    out, kv_idx, kv_num = bench.Layer(cfg).stages(q, k, v)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    B, H, N = cfg["B"], cfg["Hq"], cfg["N"]
+    M = (N + 63) // 64
+    kk = orc.keep_count(M, cfg["sparsity"])
+    assert kk == 100 and tuple(kv_idx.shape) == (B, H, M, kk) and bool((kv_num == kk).all())
+    idx_h, num_h = kv_idx.cpu().numpy(), kv_num.cpu().numpy()
+    assert (np.diff(idx_h, axis=-1) > 0).all()  # ascending, no duplicates
+    rows = [(0, 0, i) for i in (0, 1, M // 3, M // 2 + 1, M - 2, M - 1)]
+    for (b, h) in [(0, 0), (B - 1, H - 1)]:
+        qs = q_h[b:b + 1, h:h + 1].float().numpy()
+        ks = k_h[b:b + 1, h:h + 1].float().numpy()
+        vs = v_h[b:b + 1, h:h + 1].float().numpy()
+        want = orc.predictor(qs, ks, 64, cfg["sparsity"], 0.5)["mask"][0, 0]
+        got = _lists_to_dense(idx_h[b, h], num_h[b, h], M)
+        assert (got == want).mean() >= 0.999
+        assert (got & want).sum() / want.sum() >= 0.999
+        att, _ = orc.block_sparse_attention(qs, ks, vs, idx_h[b:b + 1, h:h + 1], num_h[b:b + 1, h:h + 1], 64,
+                                            False, rows=rows)
+        got_o = out[b, h].float().cpu().numpy()
+        for (_, _, i) in rows:
+            err = np.abs(got_o[64 * i:64 * (i + 1)] - att[0, 0, 64 * i:64 * (i + 1)]).max()
+            assert err <= 2e-2, (b, h, i, err)
+
+
+def _mask_agrees(got, want, kept_bar=0.99):
     assert (got == want).mean() >= 0.999
-    assert (got & want).sum() / max(1, want.sum()) >= 0.99
+    assert (got & want).sum() / max(1, want.sum()) >= kept_bar
 
 
 def test_c3_cab_attention_layer():

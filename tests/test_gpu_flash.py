@@ -76,12 +76,34 @@ def test_flash_matches_oracle(dt, B, Hq, Hkv, Nq, Nk, D, causal):
     assert torch.isfinite(lse).all()
 
 
+@pytest.mark.parametrize("dt,B,Hq,Hkv,Nq,Nk,D,causal", [
+    ("bf16", 1, 2, 2, 200, 200, 128, False),
+    ("bf16", 2, 4, 2, 1000, 1000, 64, False),
+    ("bf16", 1, 2, 2, 640, 640, 64, True),
+    ("bf16", 1, 1, 1, 4096, 4096, 128, True),
+    ("f16", 2, 3, 3, 257, 129, 64, False),
+    ("bf16", 1, 4, 4, 1, 4096, 128, False),     # one-token decode step
+])
+def test_flash_plain_matches_oracle(dt, B, Hq, Hkv, Nq, Nk, D, causal):
+    q = rand((B, Hq, Nq, D), DT[dt], 61)
+    k = rand((B, Hkv, Nk, D), DT[dt], 62)
+    v = rand((B, Hkv, Nk, D), DT[dt], 63)
+    out, lse = flash_attention_forward(q.cuda(), k.cuda(), v.cuda(), causal=causal, return_lse=True)
+    want, _ = orc.flash_attention_cumulative(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                             causal=causal, p_round=rounder(DT[dt]))
+    err = np.abs(out.double().cpu().numpy() - want).max()
+    assert err <= OUT_TOL[dt], f"max abs err {err:.3e}"
+    assert torch.isfinite(lse).all()
+    assert _lib.device_status() == 0
+
+
 def test_flash_without_scores_and_accumulation():
     q = rand((1, 2, 200, 128), torch.bfloat16, 41)
     k = rand((1, 2, 200, 128), torch.bfloat16, 42)
     v = rand((1, 2, 200, 128), torch.bfloat16, 43)
     plain = flash_attention_forward(q.cuda(), k.cuda(), v.cuda())
     out1, cum1 = flash_attention_with_cumulative_scores(q.cuda(), k.cuda(), v.cuda())
+    # the column scores are an epilogue of the same kernel: the outputs are identical
     assert torch.equal(plain, out1)
     # a second call accumulates into the same scores
     out2, cum2 = flash_attention_with_cumulative_scores(q.cuda(), k.cuda(), v.cuda(), cum1.clone())
@@ -167,3 +189,46 @@ def test_flash_matches_reference_kernel_live():
         tol = OUT_TOL["f16" if dtype == torch.float16 else "bf16"]
         assert (out.float() - rout.float()).abs().max().item() <= tol
         check_scores(cum, rcum.double().cpu().numpy())
+
+
+def test_patched_hf_attention_forward():
+    # a Qwen2-shaped module (head counts only in its config, GQA 4/2, head_dim 64): the
+    # patched forward equals projections + RoPE + plain softmax attention + o_proj, and two
+    # calls accumulate the column scores on the module
+    import types
+    from cab_attention.kernels import flash_attention_accumulate as faa
+
+    torch.manual_seed(0)
+    H, KV, D, T = 4, 2, 64, 96
+    attn = torch.nn.Module()
+    attn.head_dim = D
+    attn.config = types.SimpleNamespace(num_attention_heads=H, num_key_value_heads=KV)
+    for name, o in (("q_proj", H), ("k_proj", KV), ("v_proj", KV), ("o_proj", H)):
+        setattr(attn, name, torch.nn.Linear(H * D, o * D, bias=False))
+    attn = attn.to(torch.bfloat16).cuda()
+    layer = torch.nn.Module()
+    layer.self_attn = attn
+    model = torch.nn.Module()
+    model.model = torch.nn.Module()
+    model.model.layers = torch.nn.ModuleList([layer])
+    faa.replace_attention_with_flash(model)
+    x = torch.randn(1, T, H * D, device="cuda").to(torch.bfloat16)
+    ang = torch.arange(T, device="cuda")[:, None] * torch.rand(D // 2, device="cuda")[None, :]
+    cos = torch.cat([ang.cos(), ang.cos()], -1)[None].to(torch.bfloat16)
+    sin = torch.cat([ang.sin(), ang.sin()], -1)[None].to(torch.bfloat16)
+    with torch.no_grad():
+        out, none = attn.forward(x, (cos, sin))
+        q = attn.q_proj(x).view(1, T, H, D).transpose(1, 2)
+        k = attn.k_proj(x).view(1, T, KV, D).transpose(1, 2)
+        v = attn.v_proj(x).view(1, T, KV, D).transpose(1, 2)
+        q, k = faa.apply_rotary_pos_emb(q, k, cos, sin)
+        k, v = faa.repeat_kv(k, H // KV), faa.repeat_kv(v, H // KV)
+        p = torch.softmax(q.float() @ k.float().transpose(-1, -2) / D ** 0.5, dim=-1)
+        want = attn.o_proj((p @ v.float()).to(torch.bfloat16).transpose(1, 2).reshape(1, T, H * D))
+    assert none is None and out.shape == (1, T, H * D)
+    assert (out.float() - want.float()).abs().max().item() <= 2e-2
+    s1 = faa.get_all_cumulative_scores(model)["model.layers.0.self_attn"].clone()
+    with torch.no_grad():
+        attn.forward(x, (cos, sin))
+    s2 = faa.get_all_cumulative_scores(model)["model.layers.0.self_attn"]
+    torch.testing.assert_close(s2, 2 * s1, rtol=1e-5, atol=1e-5)

@@ -114,3 +114,11 @@ def test_dead_rank_is_detected_not_hung():
     for p in procs:
         p.join(timeout=60)
     assert rank == 0 and kind != "no error"
+
+
+def test_unit_inputs_equal_whole_batch_slices():
+    q, k, v = synthetic.make_qkv(2, 4, 2, 96, 8, torch.float32, seed=3)
+    units = [(0, 1), (1, 0)]
+    qu, ku, vu = synthetic.make_unit_qkv(units, 2, 96, 8, torch.float32, seed=3)
+    assert torch.equal(qu[0, 0:2], q[0, 2:4]) and torch.equal(qu[0, 2:4], q[1, 0:2])
+    assert torch.equal(ku[0, 0], k[0, 1]) and torch.equal(vu[0, 1], v[1, 0])

@@ -64,14 +64,25 @@ def test_noalloc_matches_workspace_entry_point_twice():
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch():
+    # real device buffers of the rejected size, so that even if the size check regressed
+    # the call would read and write memory it owns instead of a bad address
     L = _lib.lib()
     need = _lib._c_size(0)
-    N, kmax = 1 << 20, 300
-    assert L.cab_sparse_attn_workspace_size(1, 1, N, 128, 64, kmax, 2, ctypes.byref(need)) == 0
+    N, kmax, D = 1 << 20, 300, 128
+    assert L.cab_sparse_attn_workspace_size(1, 1, N, D, 64, kmax, 2, ctypes.byref(need)) == 0
     assert need.value > (16 << 20)
-    s = _lib._i64_3(N * 128, N * 128, 128)
-    fake = ctypes.c_void_p(256)
-    rc = L.cab_sparse_attn_fwd_noalloc(fake, fake, fake, fake, fake, fake, None, 1, 1, 1, N, 128,
-                                       64, kmax, s, s, s, s, 0.088, 0, 2, None)
+    q = torch.zeros(1, 1, N, D, dtype=torch.bfloat16, device="cuda")
+    k, v, out = torch.zeros_like(q), torch.zeros_like(q), torch.zeros_like(q)
+    M = N // 64
+    idx = torch.arange(kmax, dtype=torch.int32, device="cuda").repeat(M, 1).view(1, 1, M, kmax)
+    num = torch.full((1, 1, M), kmax, dtype=torch.int32, device="cuda")
+    lse = torch.zeros(1, 1, N, device="cuda")
+    s = _lib._i64_3(N * D, N * D, D)
+    rc = L.cab_sparse_attn_fwd_noalloc(q.data_ptr(), k.data_ptr(), v.data_ptr(), idx.data_ptr(),
+                                       num.data_ptr(), out.data_ptr(), lse.data_ptr(), 1, 1, 1, N, D,
+                                       64, kmax, s, s, s, s, 0.088, 0, 2,
+                                       torch.cuda.current_stream().cuda_stream)
     assert rc == 2
     assert b"16 MiB" in L.cab_last_error_string()
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
