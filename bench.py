@@ -465,6 +465,11 @@ def run_ours(args, cfg, rank, world, local_rank):
                 "frac_of_sustained": achieved / tf_sus,
                 "traffic": ATTN_TRAFFIC_BYTES.get(args.config) if world == 1 else None}
 
+    # ---- the reference's GPU attention step on the same inputs and lists: FlexAttention
+    flex = None
+    if world == 1 and args.flex and len(chunks) == 1:
+        flex = flex_compare(q, k, v, layer, lcfg, args, peak)
+
     result = None
     if rank == 0:
         cpu = None
@@ -507,10 +512,55 @@ def run_ours(args, cfg, rank, world, local_rank):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
         }
+        if flex is not None:
+            result["flex"] = flex
+            if "ms" in flex:
+                result["flex_ms"] = flex["ms"]
         if gather_ms is not None:
             result["gather_ms"] = gather_ms
             result["gather_bytes_per_rank"] = sum(g.numel() * g.element_size() for g in gbuf)
     return result
+
+
+def flex_compare(q, k, v, layer, lcfg, args, peak):
+    """Times torch's FlexAttention (compiled) on the same inputs and the same kept-block
+    lists (oracle/flex_reference.py), for the same-box bar beside attn_tc_kernel."""
+    try:
+        from oracle import flex_reference as fr
+        from cab_attention.kernels import block_sparse_attention
+        from cab_attention.kernels.sparse_attention import sparse_attention_flops
+        out, kv_idx, kv_num = layer.stages(q, k, v)
+        bm = fr.block_mask(kv_idx, kv_num, lcfg["N"], BLOCK, lcfg["causal"])
+        t0 = time.perf_counter()
+        ref = fr.attention(q, k, v, bm)
+        torch.cuda.synchronize()
+        compile_s = time.perf_counter() - t0
+        diff = (ref.float() - out.float()).abs().max().item()
+        del ref
+        for _ in range(2):
+            fr.attention(q, k, v, bm)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        o0, o1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            fr.attention(q, k, v, bm)
+        e1.record()
+        o0.record()
+        for _ in range(args.steps):
+            block_sparse_attention(q, k, v, kv_idx, kv_num, BLOCK, lcfg["causal"])
+        o1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        ours_ms = o0.elapsed_time(o1) / args.steps
+        flop = sparse_attention_flops(kv_num, BLOCK, lcfg["D"])
+        return {"ms": ms, "TFLOP/s": flop / ms / 1e9, "frac_bf16": flop / ms / 1e9 / peak,
+                "ours_ms_same_loop": ours_ms, "speedup_ours": ms / ours_ms,
+                "max_abs_diff_vs_ours": diff, "compile_s": round(compile_s, 1),
+                "what": f"torch {torch.__version__} flex_attention (torch.compile), BlockMask.from_kv_blocks "
+                        f"BLOCK_SIZE={BLOCK} from the same kv_idx / kv_num, kept blocks as full blocks"}
+    except Exception as e:  # the comparison must not take the benchmark down
+        return {"unavailable": f"{type(e).__name__}: {str(e)[:300]}"}
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum per attention launch, from ncu captures of
@@ -1177,6 +1227,8 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-baseline-seconds", type=float, default=15.0)
     ap.add_argument("--reference-step-seconds", type=float, default=6.0)
+    ap.add_argument("--no-flex", dest="flex", action="store_false",
+                    help="skip the FlexAttention comparison on the same lists (1 GPU)")
     ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
                     help="--gpus N > 1: split one layer's (batch x head) units over the ranks and "
                          "all-gather the output (strong), or give every rank its own layer (weak)")

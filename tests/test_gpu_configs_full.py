@@ -6,10 +6,9 @@ s=0.95, one planted bridge per (b, h)), configs[2] (C3: the CABAttention layer, 
 the predictor over N in {1k, 4k, 16k, 64k, 128k}, B2 H8 D128 bf16, s=0.95) and configs[4]
 (C5: GQA 32/8, B1 N65536 D128 bf16, causal, s=0.99, four planted bridges). Checked by
 size-independent properties: every planted bridge is kept; on sampled heads the block
-mask agrees with the float64 oracle (>= 99.9 % of all blocks; of kept blocks >= 99.9 % for
-the north_star layer, C2 and C5, where 99.945-99.99 % was measured, and >= 99 % for C3 and
-the C4 sweep, whose small-M cases keep few blocks per row: fp16 triangle products move a
-few near-tied blocks); attention on sampled query blocks
+mask agrees with the float64 oracle on >= 99.9 % of all blocks and of kept blocks (fp16
+triangle products move a few near-tied blocks: 99.94-100 % of kept blocks measured on every
+configuration); attention on sampled query blocks
 matches the oracle given the same lists (max abs error <= 2e-2); the layer output on
 sampled rows matches the output projection of the oracle attention (max abs error
 <= 2e-3 at these weight scales)."""
@@ -107,7 +106,7 @@ def test_north_star_layer():
             assert err <= 2e-2, (b, h, i, err)
 
 
-def _mask_agrees(got, want, kept_bar=0.99):
+def _mask_agrees(got, want, kept_bar=0.999):
     assert (got == want).mean() >= 0.999
     assert (got & want).sum() / max(1, want.sum()) >= kept_bar
 
