@@ -178,6 +178,22 @@ struct Cfg {
 constexpr int kSBufs = 3;
 constexpr uint32_t kTmemO = 384;
 
+// One completion signal per MMA group where the rings allow it. After the first
+// tcgen05.commit of a group every further commit costs the tensor pipe time (about 86
+// clocks measured on B200), so:
+//  * with at most kSBufs K stages the producer frees a K stage on s_full (S(g) completed)
+//    instead of a separate k_empty commit: S(g + 3), the next phase of the same barrier,
+//    needs K(g + 3), which is loaded after that wait, so the producer never falls a phase
+//    behind;
+//  * with exactly kSBufs V stages, V stage, S/P buffer and PV-completion barrier coincide:
+//    buf_free[g % 3] (PV(g) completed) also frees V stage g % 3 and feeds the completion
+//    tracker, replacing the v_empty and o_ready commits.
+template <class C>
+struct Signals {
+  static constexpr bool kKOnSFull = C::kKStages <= kSBufs;
+  static constexpr bool kPvOneCommit = C::kVStages == kSBufs;
+};
+
 // Warp 0: TMA producer; warp 1: issues S = Q K^T; warps 2-9: softmax; warp 10: issues
 // O += P V; warp 11: PV completion tracker. Two issuing threads keep the tensor pipe
 // queued: while one blocks on a full MMA queue, the other's group is already waiting
@@ -196,10 +212,13 @@ __device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
 // sound while no arrival for a later phase can overtake one for the current phase. Each
 // barrier below is therefore waited phase after phase by one consumer, or made safe by a
 // dependency: P(g) arrives on p_full[g % 3], and a warp can only reach tile g + 3 after
-// PV(g) consumed p_full(g). PV completions (o_ready[g & 1]) are consumed in order by
-// warp 11 alone, which publishes their count in `pv_seen`; the PV issuer starts PV(g)
-// only once PV(g - 2) has been seen, so o_ready never runs two phases ahead of warp 11,
-// while PV(g - 1) and PV(g) can still be queued together. Softmax threads wait on that
+// PV(g) consumed p_full(g). PV completions are consumed in order by warp 11 alone, which
+// publishes their count in `pv_seen`: on buf_free[g % 3] where that barrier is the only
+// PV signal (the PV issuer then starts PV(g) once PV(g - 3) has been seen), else on
+// o_ready[g & 1] (PV(g) once PV(g - 2) has been seen), so the barrier never runs two
+// phases ahead of warp 11 while consecutive PVs can still be queued together. The
+// producer's waits on s_full and buf_free are safe for the same reason: the next phase
+// of the barrier needs the very tile it is about to load. Softmax threads wait on the
 // count only when they must rescale O (rare) and in the epilogue.
 constexpr int kSoftmaxWarps = 8;
 constexpr int kPvWarp = 2 + kSoftmaxWarps;
@@ -374,7 +393,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             }
           }
           const int ks = kt % C::kKStages;
-          if (!mbar_wait(&k_empty[ks], ((kt / C::kKStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
+          if constexpr (Signals<C>::kKOnSFull) {
+            // K stage ks is free once S(kt - kKStages), its last reader, has completed
+            if (kt >= static_cast<uint32_t>(C::kKStages)) {
+              const uint32_t kd = kt - C::kKStages;
+              if (!mbar_wait(&s_full[kd % kSBufs], (kd / kSBufs) & 1, abort_flag)) { ok = false; break; }
+            }
+          } else {
+            if (!mbar_wait(&k_empty[ks], ((kt / C::kKStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
+          }
           mbar_arrive_expect_tx(&k_full[ks], C::kKBytes);
           uint8_t* dk = sK + ks * C::kKBytes;
 #pragma unroll
@@ -384,7 +411,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
           ++kt;
           const int vs = vt % C::kVStages;
-          if (!mbar_wait(&v_empty[vs], ((vt / C::kVStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
+          // V stage vs is free once PV(vt - kVStages) has completed
+          uint64_t* v_free = Signals<C>::kPvOneCommit ? &buf_free[vs] : &v_empty[vs];
+          if (!mbar_wait(v_free, ((vt / C::kVStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&v_full[vs], C::kVBytes);
           uint8_t* dv = sV + vs * C::kVBytes;
 #pragma unroll
@@ -435,7 +464,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const uint64_t off = (kk >> 2) * (16384 >> 4) + (kk & 3) * (32 >> 4);
             mma_f16_ss(d_s, dq + off, dk + off, idesc_s, kk > 0 ? 1u : 0u);
           }
-          mma_commit(&k_empty[ks]);
+          if constexpr (!Signals<C>::kKOnSFull) mma_commit(&k_empty[ks]);
           mma_commit(&s_full[buf]);
           ++kt;
         }
@@ -469,7 +498,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (!mbar_wait(&p_full[g % kSBufs], (g / kSBufs) & 1, abort_flag) ||
               !mbar_wait(&v_full[vs], (vt / C::kVStages) & 1, abort_flag)) { ok = false; break; }
           if (t == 0 && gi > 0 && !mbar_wait(o_free, (gi - 1) & 1, abort_flag)) { ok = false; break; }
-          if (g >= 2 && !counter_wait(pv_seen, g - 1, abort_flag)) { ok = false; break; }
+          // the tracker must have taken the previous phase of the completion barrier PV(g) will
+          // signal: PV(g - 3) on buf_free[g % 3], or PV(g - 2) on o_ready[g & 1]
+          if constexpr (Signals<C>::kPvOneCommit) {
+            if (g >= 3 && !counter_wait(pv_seen, g - 2, abort_flag)) { ok = false; break; }
+          } else {
+            if (g >= 2 && !counter_wait(pv_seen, g - 1, abort_flag)) { ok = false; break; }
+          }
           tc_fence_after_sync();
           const uint64_t dv = dV + static_cast<uint64_t>((vs * C::kVBytes) >> 4);
           const uint32_t pt = tmem + (g % kSBufs) * 128;
@@ -477,8 +512,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int kk = 0; kk < 8; ++kk)
             mma_f16_ts(tmem_o, pt + (kk >> 2) * 64 + (kk & 3) * 8,
                        dv + static_cast<uint64_t>(kk * (2048 >> 4)), idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
-          mma_commit(&v_empty[vs]);
-          mma_commit(&o_ready[g & 1]);
+          if constexpr (!Signals<C>::kPvOneCommit) {
+            mma_commit(&v_empty[vs]);
+            mma_commit(&o_ready[g & 1]);
+          }
           mma_commit(&buf_free[g % kSBufs]);
           ++vt;
         }
@@ -502,7 +539,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (item + gridDim.x < p.items) T_next = item_tiles<kDense>(p, item + gridDim.x);
         for (int t = 0; t < T; ++t) {
           const uint32_t g = gt + t;
-          if (!mbar_wait(&o_ready[g & 1], (g >> 1) & 1, abort_flag)) { ok = false; break; }
+          const bool okt = Signals<C>::kPvOneCommit ? mbar_wait(&buf_free[g % kSBufs], (g / kSBufs) & 1, abort_flag)
+                                                     : mbar_wait(&o_ready[g & 1], (g >> 1) & 1, abort_flag);
+          if (!okt) { ok = false; break; }
           counter_store(pv_seen, g + 1);
         }
         gt += T;
