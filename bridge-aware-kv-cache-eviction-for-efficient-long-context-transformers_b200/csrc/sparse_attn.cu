@@ -10,11 +10,11 @@
 //    this item finishes) and the K and V tiles with TMA (128-byte swizzle) into
 //    shared-memory rings. One thread of warp 1 issues S = Q K^T (M=128, N=128, K=D; both
 //    operands K-major from shared memory) into one of three TMEM S buffers; one thread of
-//    warp 10 issues O += P V (P from TMEM where the softmax wrote it over its S, V read
+//    warp 2 issues O += P V (P from TMEM where the softmax wrote it over its S, V read
 //    MN-major from its natural [keys, D] layout; M=128, N=D, K=128). Three buffers keep
-//    S(g+1), S(g+2) and PV(g-1) in flight while tile g is in the softmax. Warp 11 consumes
+//    S(g+1), S(g+2) and PV(g-1) in flight while tile g is in the softmax. Warp 3 consumes
 //    the PV completions in order and publishes their count.
-//  * Warps 2-9, two per row (one per 64-key block of the tile): tcgen05.ld of the S row
+//  * Warps 4-11, two per row (one per 64-key block of the tile): tcgen05.ld of the S row
 //    half, exact masking (union flags, causal token mask, sequence end), online softmax
 //    in the exp2 domain with a lazy rescale of O (only when the running max grows by more
 //    than 2^8), P stored to TMEM over the S columns it came from, and the final O / l
@@ -221,9 +221,17 @@ __device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
 // of the barrier needs the very tile it is about to load. Softmax threads wait on the
 // count only when they must rescale O (rare) and in the epilogue.
 constexpr int kSoftmaxWarps = 8;
-constexpr int kPvWarp = 2 + kSoftmaxWarps;
-constexpr int kTrackWarp = kPvWarp + 1;
-constexpr int kAttnThreads = 32 * (kTrackWarp + 1);
+constexpr int kPvWarp = 2;
+constexpr int kTrackWarp = 3;
+constexpr int kFirstSoftmaxWarp = 4;
+constexpr int kAttnThreads = 32 * (kFirstSoftmaxWarp + kSoftmaxWarps);
+// Register split of the sparse kernel (setmaxnreg): warpgroup 0 (producer, issuers,
+// tracker) hands registers to the two softmax warpgroups (measured 4-5 % faster on B200
+// than the even 168 / 168 split). 128 x (kRegsLow + 2 x kRegsHigh) must not exceed the
+// launch's 384 x 168; the host checks the kernel's register count before each launch.
+constexpr int kRegsLow = 72, kRegsHigh = 216;
+constexpr int kRegsNeeded = (128 * (kRegsLow + 2 * kRegsHigh) + kAttnThreads - 1) / kAttnThreads;
+static_assert(kRegsNeeded <= 168, "register split exceeds the launch's registers");
 
 struct Params {
   int32_t B, Hq, Hkv, Nq, Nk, M, P;  // sparse: Nq == Nk == N; dense: P = query blocks of 128 rows
@@ -354,209 +362,216 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem_o = tmem + kTmemO;
   const int G = p.Hq / p.Hkv;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer (Q, K, V)
-    if (lane == 0) {
-      uint32_t gi = 0, kt = 0, vt = 0;
-      bool ok = true;
-      // Tile counts are read one item ahead and list entries one tile ahead, so no list
-      // read sits between a free stage and its TMA issue.
-      int T_next = static_cast<int64_t>(blockIdx.x) < p.items ? item_tiles<kDense>(p, blockIdx.x) : 0;
-      for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
-        const int T = T_next;
-        if (item + gridDim.x < p.items) T_next = item_tiles<kDense>(p, item + gridDim.x);
-        if (T == 0) continue;
-        const uint32_t it = static_cast<uint32_t>(item);
-        const int bh = static_cast<int>(it / static_cast<uint32_t>(p.P));
-        const int pr = static_cast<int>(it - static_cast<uint32_t>(bh) * static_cast<uint32_t>(p.P));
-        const int b = bh / p.Hq, h = bh % p.Hq, hk = h / G;
-        const uint32_t* ul = p.ulist + item * p.stride;
-        uint32_t e0 = 0u, e1 = 0u;
-        if constexpr (!kDense) {
-          e0 = ld_nc_u32(ul);
-          e1 = ld_nc_u32(ul + 1);
-        }
-        const int qs = static_cast<int>(gi % C::kQStages);
-        if (!mbar_wait(&q_empty[qs], ((gi / C::kQStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
-        mbar_arrive_expect_tx(&q_full[qs], C::kQBytes);
-#pragma unroll
-        for (int a = 0; a < C::kAtoms; ++a)
-          tma_load_4d(sQ + qs * C::kQBytes + a * 16384, &qmap, &q_full[qs], 64 * a, 128 * pr, h, b);
-        ++gi;
-        for (int t = 0; t < T; ++t) {
-          const int j0 = kDense ? 2 * t : static_cast<int>(e0 & kIdxMask);
-          const int j1 = kDense ? 2 * t + 1 : static_cast<int>(e1 & kIdxMask);
+  if (warp < kFirstSoftmaxWarp) {
+    // warpgroup 0: TMA producer, S issuer, PV issuer, PV-completion tracker
+    if constexpr (!kDense) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
+    if (warp == 0) {
+      // ------------------------------------------------------------ TMA producer (Q, K, V)
+      if (lane == 0) {
+        uint32_t gi = 0, kt = 0, vt = 0;
+        bool ok = true;
+        // Tile counts are read one item ahead and list entries one tile ahead, so no list
+        // read sits between a free stage and its TMA issue.
+        int T_next = static_cast<int64_t>(blockIdx.x) < p.items ? item_tiles<kDense>(p, blockIdx.x) : 0;
+        for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
+          const int T = T_next;
+          if (item + gridDim.x < p.items) T_next = item_tiles<kDense>(p, item + gridDim.x);
+          if (T == 0) continue;
+          const uint32_t it = static_cast<uint32_t>(item);
+          const int bh = static_cast<int>(it / static_cast<uint32_t>(p.P));
+          const int pr = static_cast<int>(it - static_cast<uint32_t>(bh) * static_cast<uint32_t>(p.P));
+          const int b = bh / p.Hq, h = bh % p.Hq, hk = h / G;
+          const uint32_t* ul = p.ulist + item * p.stride;
+          uint32_t e0 = 0u, e1 = 0u;
           if constexpr (!kDense) {
-            if (t + 1 < T) {
-              e0 = ld_nc_u32(ul + 2 * t + 2);
-              e1 = ld_nc_u32(ul + 2 * t + 3);
+            e0 = ld_nc_u32(ul);
+            e1 = ld_nc_u32(ul + 1);
+          }
+          const int qs = static_cast<int>(gi % C::kQStages);
+          if (!mbar_wait(&q_empty[qs], ((gi / C::kQStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&q_full[qs], C::kQBytes);
+  #pragma unroll
+          for (int a = 0; a < C::kAtoms; ++a)
+            tma_load_4d(sQ + qs * C::kQBytes + a * 16384, &qmap, &q_full[qs], 64 * a, 128 * pr, h, b);
+          ++gi;
+          for (int t = 0; t < T; ++t) {
+            const int j0 = kDense ? 2 * t : static_cast<int>(e0 & kIdxMask);
+            const int j1 = kDense ? 2 * t + 1 : static_cast<int>(e1 & kIdxMask);
+            if constexpr (!kDense) {
+              if (t + 1 < T) {
+                e0 = ld_nc_u32(ul + 2 * t + 2);
+                e1 = ld_nc_u32(ul + 2 * t + 3);
+              }
             }
-          }
-          const int ks = kt % C::kKStages;
-          if constexpr (Signals<C>::kKOnSFull) {
-            // K stage ks is free once S(kt - kKStages), its last reader, has completed
-            if (kt >= static_cast<uint32_t>(C::kKStages)) {
-              const uint32_t kd = kt - C::kKStages;
-              if (!mbar_wait(&s_full[kd % kSBufs], (kd / kSBufs) & 1, abort_flag)) { ok = false; break; }
+            const int ks = kt % C::kKStages;
+            if constexpr (Signals<C>::kKOnSFull) {
+              // K stage ks is free once S(kt - kKStages), its last reader, has completed
+              if (kt >= static_cast<uint32_t>(C::kKStages)) {
+                const uint32_t kd = kt - C::kKStages;
+                if (!mbar_wait(&s_full[kd % kSBufs], (kd / kSBufs) & 1, abort_flag)) { ok = false; break; }
+              }
+            } else {
+              if (!mbar_wait(&k_empty[ks], ((kt / C::kKStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
             }
-          } else {
-            if (!mbar_wait(&k_empty[ks], ((kt / C::kKStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
+            mbar_arrive_expect_tx(&k_full[ks], C::kKBytes);
+            uint8_t* dk = sK + ks * C::kKBytes;
+  #pragma unroll
+            for (int a = 0; a < C::kAtoms; ++a) {
+              tma_load_4d(dk + a * 16384, &kmap, &k_full[ks], 64 * a, 64 * j0, hk, b);
+              tma_load_4d(dk + a * 16384 + 8192, &kmap, &k_full[ks], 64 * a, 64 * j1, hk, b);
+            }
+            ++kt;
+            const int vs = vt % C::kVStages;
+            // V stage vs is free once PV(vt - kVStages) has completed
+            uint64_t* v_free = Signals<C>::kPvOneCommit ? &buf_free[vs] : &v_empty[vs];
+            if (!mbar_wait(v_free, ((vt / C::kVStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
+            mbar_arrive_expect_tx(&v_full[vs], C::kVBytes);
+            uint8_t* dv = sV + vs * C::kVBytes;
+  #pragma unroll
+            for (int a = 0; a < C::kAtoms; ++a) {
+              tma_load_4d(dv + a * 16384, &vmap, &v_full[vs], 64 * a, 64 * j0, hk, b);
+              tma_load_4d(dv + a * 16384 + 8192, &vmap, &v_full[vs], 64 * a, 64 * j1, hk, b);
+            }
+            ++vt;
           }
-          mbar_arrive_expect_tx(&k_full[ks], C::kKBytes);
-          uint8_t* dk = sK + ks * C::kKBytes;
-#pragma unroll
-          for (int a = 0; a < C::kAtoms; ++a) {
-            tma_load_4d(dk + a * 16384, &kmap, &k_full[ks], 64 * a, 64 * j0, hk, b);
-            tma_load_4d(dk + a * 16384 + 8192, &kmap, &k_full[ks], 64 * a, 64 * j1, hk, b);
-          }
-          ++kt;
-          const int vs = vt % C::kVStages;
-          // V stage vs is free once PV(vt - kVStages) has completed
-          uint64_t* v_free = Signals<C>::kPvOneCommit ? &buf_free[vs] : &v_empty[vs];
-          if (!mbar_wait(v_free, ((vt / C::kVStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&v_full[vs], C::kVBytes);
-          uint8_t* dv = sV + vs * C::kVBytes;
-#pragma unroll
-          for (int a = 0; a < C::kAtoms; ++a) {
-            tma_load_4d(dv + a * 16384, &vmap, &v_full[vs], 64 * a, 64 * j0, hk, b);
-            tma_load_4d(dv + a * 16384 + 8192, &vmap, &v_full[vs], 64 * a, 64 * j1, hk, b);
-          }
-          ++vt;
+        }
+        if (!ok) {
+          // bounded drain of the loads this thread may still have in flight
+          for (int s = 0; s < C::kKStages; ++s) (void)mbar_wait(&k_full[s], ((kt + s) / C::kKStages) & 1, nullptr);
         }
       }
-      if (!ok) {
-        // bounded drain of the loads this thread may still have in flight
-        for (int s = 0; s < C::kKStages; ++s) (void)mbar_wait(&k_full[s], ((kt + s) / C::kKStages) & 1, nullptr);
-      }
-    }
-    __syncwarp();
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ S = Q K^T issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = make_idesc_f16(128, 128, kBF16 ? 1 : 0, 0, 0);
-      // Descriptors are built once; per stage and K step only the 14-bit start-address
-      // field (16-byte units, shared memory < 256 KB so it never carries) is advanced.
-      const uint64_t dQ = make_smem_desc(smem_u32(sQ), 16, 1024, 2);
-      const uint64_t dK = make_smem_desc(smem_u32(sK), 16, 1024, 2);
-      uint32_t gi = 0, kt = 0, gt = 0;
-      bool ok = true;
-      int T_next = static_cast<int64_t>(blockIdx.x) < p.items ? item_tiles<kDense>(p, blockIdx.x) : 0;
-      for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
-        const int T = T_next;
-        if (item + gridDim.x < p.items) T_next = item_tiles<kDense>(p, item + gridDim.x);
-        if (T == 0) continue;
-        const int qs = static_cast<int>(gi % C::kQStages);
-        if (!mbar_wait(&q_full[qs], (gi / C::kQStages) & 1, abort_flag)) { ok = false; break; }
-        tc_fence_after_sync();
-        const uint64_t dq = dQ + static_cast<uint64_t>((qs * C::kQBytes) >> 4);
-        for (int t = 0; t < T; ++t) {
-          // S(g) = Q K(g)^T into buffer g % 3 once PV(g - 3) (which read P(g - 3) there)
-          // has completed; Q and K from shared memory (K-major)
-          const uint32_t g = gt + t, buf = g % kSBufs;
-          const int ks = kt % C::kKStages;
-          if (!mbar_wait(&buf_free[buf], ((g / kSBufs) & 1) ^ 1, abort_flag) ||
-              !mbar_wait(&k_full[ks], (kt / C::kKStages) & 1, abort_flag)) { ok = false; break; }
+      __syncwarp();
+    } else if (warp == 1) {
+      // ------------------------------------------------------------ S = Q K^T issuer
+      if (lane == 0) {
+        constexpr uint32_t idesc_s = make_idesc_f16(128, 128, kBF16 ? 1 : 0, 0, 0);
+        // Descriptors are built once; per stage and K step only the 14-bit start-address
+        // field (16-byte units, shared memory < 256 KB so it never carries) is advanced.
+        const uint64_t dQ = make_smem_desc(smem_u32(sQ), 16, 1024, 2);
+        const uint64_t dK = make_smem_desc(smem_u32(sK), 16, 1024, 2);
+        uint32_t gi = 0, kt = 0, gt = 0;
+        bool ok = true;
+        int T_next = static_cast<int64_t>(blockIdx.x) < p.items ? item_tiles<kDense>(p, blockIdx.x) : 0;
+        for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
+          const int T = T_next;
+          if (item + gridDim.x < p.items) T_next = item_tiles<kDense>(p, item + gridDim.x);
+          if (T == 0) continue;
+          const int qs = static_cast<int>(gi % C::kQStages);
+          if (!mbar_wait(&q_full[qs], (gi / C::kQStages) & 1, abort_flag)) { ok = false; break; }
           tc_fence_after_sync();
-          const uint64_t dk = dK + static_cast<uint64_t>((ks * C::kKBytes) >> 4);
-          const uint32_t d_s = tmem + buf * 128;
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint64_t off = (kk >> 2) * (16384 >> 4) + (kk & 3) * (32 >> 4);
-            mma_f16_ss(d_s, dq + off, dk + off, idesc_s, kk > 0 ? 1u : 0u);
+          const uint64_t dq = dQ + static_cast<uint64_t>((qs * C::kQBytes) >> 4);
+          for (int t = 0; t < T; ++t) {
+            // S(g) = Q K(g)^T into buffer g % 3 once PV(g - 3) (which read P(g - 3) there)
+            // has completed; Q and K from shared memory (K-major)
+            const uint32_t g = gt + t, buf = g % kSBufs;
+            const int ks = kt % C::kKStages;
+            // K lands well ahead; the buffer's release (PV(g - 3)) is the event waited on last
+            if (!mbar_wait(&k_full[ks], (kt / C::kKStages) & 1, abort_flag) ||
+                !mbar_wait(&buf_free[buf], ((g / kSBufs) & 1) ^ 1, abort_flag)) { ok = false; break; }
+            tc_fence_after_sync();
+            const uint64_t dk = dK + static_cast<uint64_t>((ks * C::kKBytes) >> 4);
+            const uint32_t d_s = tmem + buf * 128;
+  #pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint64_t off = (kk >> 2) * (16384 >> 4) + (kk & 3) * (32 >> 4);
+              mma_f16_ss(d_s, dq + off, dk + off, idesc_s, kk > 0 ? 1u : 0u);
+            }
+            if constexpr (!Signals<C>::kKOnSFull) mma_commit(&k_empty[ks]);
+            mma_commit(&s_full[buf]);
+            ++kt;
           }
-          if constexpr (!Signals<C>::kKOnSFull) mma_commit(&k_empty[ks]);
-          mma_commit(&s_full[buf]);
-          ++kt;
+          if (!ok) break;
+          mma_commit(&q_empty[qs]);
+          gt += T;
+          ++gi;
         }
-        if (!ok) break;
-        mma_commit(&q_empty[qs]);
-        gt += T;
-        ++gi;
+        if (gi > 0) {
+          mma_commit(&drain[0]);
+          (void)mbar_wait(&drain[0], 0, nullptr);
+        }
       }
-      if (gi > 0) {
-        mma_commit(&drain[0]);
-        (void)mbar_wait(&drain[0], 0, nullptr);
-      }
-    }
-    __syncwarp();
-  } else if (warp == kPvWarp) {
-    // ------------------------------------------------------------ O += P V issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_o = make_idesc_f16(128, D, kBF16 ? 1 : 0, 0, 1);
-      const uint64_t dV = make_smem_desc(smem_u32(sV), 16384, 1024, 2);
-      uint32_t gi = 0, vt = 0, gt = 0;
-      bool ok = true;
-      int T_next = static_cast<int64_t>(blockIdx.x) < p.items ? item_tiles<kDense>(p, blockIdx.x) : 0;
-      for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
-        const int T = T_next;
-        if (item + gridDim.x < p.items) T_next = item_tiles<kDense>(p, item + gridDim.x);
-        if (T == 0) continue;
-        for (int t = 0; t < T; ++t) {
-          // P from TMEM (in its S buffer), V from shared memory (MN-major)
-          const uint32_t g = gt + t;
-          const int vs = vt % C::kVStages;
-          if (!mbar_wait(&p_full[g % kSBufs], (g / kSBufs) & 1, abort_flag) ||
-              !mbar_wait(&v_full[vs], (vt / C::kVStages) & 1, abort_flag)) { ok = false; break; }
-          if (t == 0 && gi > 0 && !mbar_wait(o_free, (gi - 1) & 1, abort_flag)) { ok = false; break; }
-          // the tracker must have taken the previous phase of the completion barrier PV(g) will
-          // signal: PV(g - 3) on buf_free[g % 3], or PV(g - 2) on o_ready[g & 1]
-          if constexpr (Signals<C>::kPvOneCommit) {
-            if (g >= 3 && !counter_wait(pv_seen, g - 2, abort_flag)) { ok = false; break; }
-          } else {
-            if (g >= 2 && !counter_wait(pv_seen, g - 1, abort_flag)) { ok = false; break; }
+      __syncwarp();
+    } else if (warp == kPvWarp) {
+      // ------------------------------------------------------------ O += P V issuer
+      if (lane == 0) {
+        constexpr uint32_t idesc_o = make_idesc_f16(128, D, kBF16 ? 1 : 0, 0, 1);
+        const uint64_t dV = make_smem_desc(smem_u32(sV), 16384, 1024, 2);
+        uint32_t gi = 0, vt = 0, gt = 0;
+        bool ok = true;
+        int T_next = static_cast<int64_t>(blockIdx.x) < p.items ? item_tiles<kDense>(p, blockIdx.x) : 0;
+        for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
+          const int T = T_next;
+          if (item + gridDim.x < p.items) T_next = item_tiles<kDense>(p, item + gridDim.x);
+          if (T == 0) continue;
+          for (int t = 0; t < T; ++t) {
+            // P from TMEM (in its S buffer), V from shared memory (MN-major)
+            const uint32_t g = gt + t;
+            const int vs = vt % C::kVStages;
+            // Everything that is normally ready early is waited on first, so that P(g), the
+            // event on the critical path, is the last wait before the issue.
+            if (!mbar_wait(&v_full[vs], (vt / C::kVStages) & 1, abort_flag)) { ok = false; break; }
+            if (t == 0 && gi > 0 && !mbar_wait(o_free, (gi - 1) & 1, abort_flag)) { ok = false; break; }
+            // the tracker must have taken the previous phase of the completion barrier PV(g) will
+            // signal: PV(g - 3) on buf_free[g % 3], or PV(g - 2) on o_ready[g & 1]
+            if constexpr (Signals<C>::kPvOneCommit) {
+              if (g >= 3 && !counter_wait(pv_seen, g - 2, abort_flag)) { ok = false; break; }
+            } else {
+              if (g >= 2 && !counter_wait(pv_seen, g - 1, abort_flag)) { ok = false; break; }
+            }
+            if (!mbar_wait(&p_full[g % kSBufs], (g / kSBufs) & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after_sync();
+            const uint64_t dv = dV + static_cast<uint64_t>((vs * C::kVBytes) >> 4);
+            const uint32_t pt = tmem + (g % kSBufs) * 128;
+  #pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              mma_f16_ts(tmem_o, pt + (kk >> 2) * 64 + (kk & 3) * 8,
+                         dv + static_cast<uint64_t>(kk * (2048 >> 4)), idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
+            if constexpr (!Signals<C>::kPvOneCommit) {
+              mma_commit(&v_empty[vs]);
+              mma_commit(&o_ready[g & 1]);
+            }
+            mma_commit(&buf_free[g % kSBufs]);
+            ++vt;
           }
-          tc_fence_after_sync();
-          const uint64_t dv = dV + static_cast<uint64_t>((vs * C::kVBytes) >> 4);
-          const uint32_t pt = tmem + (g % kSBufs) * 128;
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_f16_ts(tmem_o, pt + (kk >> 2) * 64 + (kk & 3) * 8,
-                       dv + static_cast<uint64_t>(kk * (2048 >> 4)), idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
-          if constexpr (!Signals<C>::kPvOneCommit) {
-            mma_commit(&v_empty[vs]);
-            mma_commit(&o_ready[g & 1]);
+          if (!ok) break;
+          gt += T;
+          ++gi;
+        }
+        if (gi > 0) {
+          mma_commit(&drain[1]);
+          (void)mbar_wait(&drain[1], 0, nullptr);
+        }
+      }
+      __syncwarp();
+    } else if (warp == kTrackWarp) {
+      if (lane == 0) {
+        uint32_t gt = 0;
+        bool ok = true;
+        int T_next = static_cast<int64_t>(blockIdx.x) < p.items ? item_tiles<kDense>(p, blockIdx.x) : 0;
+        for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
+          const int T = T_next;
+          if (item + gridDim.x < p.items) T_next = item_tiles<kDense>(p, item + gridDim.x);
+          for (int t = 0; t < T; ++t) {
+            const uint32_t g = gt + t;
+            const bool okt = Signals<C>::kPvOneCommit ? mbar_wait(&buf_free[g % kSBufs], (g / kSBufs) & 1, abort_flag)
+                                                       : mbar_wait(&o_ready[g & 1], (g >> 1) & 1, abort_flag);
+            if (!okt) { ok = false; break; }
+            counter_store(pv_seen, g + 1);
           }
-          mma_commit(&buf_free[g % kSBufs]);
-          ++vt;
+          gt += T;
         }
-        if (!ok) break;
-        gt += T;
-        ++gi;
       }
-      if (gi > 0) {
-        mma_commit(&drain[1]);
-        (void)mbar_wait(&drain[1], 0, nullptr);
-      }
+      __syncwarp();
     }
-    __syncwarp();
-  } else if (warp == kTrackWarp) {
-    if (lane == 0) {
-      uint32_t gt = 0;
-      bool ok = true;
-      int T_next = static_cast<int64_t>(blockIdx.x) < p.items ? item_tiles<kDense>(p, blockIdx.x) : 0;
-      for (int64_t item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
-        const int T = T_next;
-        if (item + gridDim.x < p.items) T_next = item_tiles<kDense>(p, item + gridDim.x);
-        for (int t = 0; t < T; ++t) {
-          const uint32_t g = gt + t;
-          const bool okt = Signals<C>::kPvOneCommit ? mbar_wait(&buf_free[g % kSBufs], (g / kSBufs) & 1, abort_flag)
-                                                     : mbar_wait(&o_ready[g & 1], (g >> 1) & 1, abort_flag);
-          if (!okt) { ok = false; break; }
-          counter_store(pv_seen, g + 1);
-        }
-        gt += T;
-      }
-    }
-    __syncwarp();
   } else {
+    if constexpr (!kDense) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
     // ------------------------------------------------------------ softmax + epilogue
-    // (warps 2 .. kPvWarp - 1)
-    // Warp w (2..9) owns TMEM lane quadrant w & 3 (rows 32*(w&3) .. +31 of the 128-row
-    // tile) and key block kb = (w - 2) / 4 of every 128-key tile (columns 64*kb .. +63).
+    // Warp w (4..11) owns TMEM lane quadrant w & 3 (rows 32*(w&3) .. +31 of the 128-row
+    // tile) and key block kb = (w - 4) / 4 of every 128-key tile (columns 64*kb .. +63).
     // The two threads of a row swap partial row maxima through shared memory
-    // (double-buffered by tile parity) under a 64-thread named barrier.
+    // (double-buffered by exchange parity) under a 64-thread named barrier.
     const int quad = warp & 3;
-    const int kb = (warp - 2) >> 2;
+    const int kb = (warp - kFirstSoftmaxWarp) >> 2;
     const int r = quad * 32 + lane;
     const int half = r >> 6;
     // Row-pair exchanges (tile maxima, final row sums) alternate between two buffers; `xc`
@@ -1030,6 +1045,17 @@ template <int D, bool kBF16, bool kDense>
 static int launch_tc(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const CUtensorMap& om,
                      const Params& p, int grid, cudaStream_t st) {
   auto kern = attn_tc_kernel<D, kBF16, kDense>;
+  if constexpr (!kDense) {
+    // The softmax warpgroups raise their register limit with setmaxnreg from the pool the
+    // CTA was launched with; a build that gave the kernel fewer registers would make that
+    // wait forever, so it is refused here.
+    static const int regs = [&] {
+      cudaFuncAttributes fa{};
+      return cudaFuncGetAttributes(&fa, kern) == cudaSuccess ? fa.numRegs : -1;
+    }();
+    if (regs < kRegsNeeded)
+      return fail(CAB_ERR_LAUNCH, "attn_tc_kernel built with %d registers per thread, needs %d", regs, kRegsNeeded);
+  }
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D, kDense>::kSmem);
   kern<<<grid, kAttnThreads, Cfg<D, kDense>::kSmem, st>>>(qm, km, vm, om, p);
   return check_launch("attn_tc_kernel");
