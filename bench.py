@@ -565,11 +565,11 @@ def flex_compare(q, k, v, layer, lcfg, args, peak):
 
 # dram__bytes_read.sum + dram__bytes_write.sum per attention launch, from ncu captures of
 # attn_tc_kernel<128, bf16, sparse> on the north_star shape with 4 of its 16 (b, h) units
-# (409.461 MB read + 116.139 MB written) and of attn_tc_kernel<64, bf16, sparse> in the
+# (409.530 MB read + 117.187 MB written) and of attn_tc_kernel<64, bf16, sparse> in the
 # configs[2] layer with 1 of its 2 batches (500.599 MB read + 114.063 MB written). DRAM
 # traffic is per unit (each unit reads its own Q/K/V once and writes its own O), so the
 # full launches are scaled by 16 / 4 and by 2.
-ATTN_TRAFFIC_BYTES = {"ns": (409.461248e6 + 116.139264e6) * 4,
+ATTN_TRAFFIC_BYTES = {"ns": (409.530112e6 + 117.187328e6) * 4,
                       "c3": (500.599296e6 + 114.062592e6) * 2}
 
 
