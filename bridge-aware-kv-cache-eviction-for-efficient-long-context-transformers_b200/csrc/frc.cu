@@ -45,10 +45,20 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kABytes = kTileM * kTileK * 2;  // 16 KB
 constexpr int kBBytes = kTileN * kTileK * 2;  // 32 KB
 constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align slack*/ + 256 /*barriers*/;
 constexpr float kEps = 1e-8f;
 
 enum Mode { kAffinity = 0, kTriangle = 1 };
+
+// Shared memory per mode. GEMM 1 (K = D <= 128, one or two K blocks per tile) runs a
+// 2-stage ring and stages its f16 Direct tile for TMA stores: each epilogue warp owns two
+// 32-row x 64-column boxes (128-byte rows, 128-byte swizzle) = 8 KB. GEMM 2 runs 4 stages.
+template <int kMode>
+struct Ring {
+  static constexpr int kStages = kMode == kAffinity ? 2 : frc::kStages;
+  static constexpr int kBoxBytes = 32 * 64 * 2;
+  static constexpr int kStagingBytes = kMode == kAffinity ? kEpiWarps * 2 * kBoxBytes : 0;
+  static constexpr int kSmem = kStages * kStageBytes + kStagingBytes + 1024 /*align slack*/ + 256 /*barriers*/;
+};
 
 struct Params {
   int32_t BH, Hq, Hkv, M, D, Mp;  // Mp: leading dimension (elements) of the Direct buffers
@@ -63,6 +73,7 @@ struct Params {
   float* frc;         // [BH, M, M]
   float* affinity;    // [BH, M, M] or null
   float* redundancy;  // [BH, M, M] or null
+  int32_t direct_tma;  // GEMM 1: Direct (hi only) leaves through staged TMA stores
 };
 
 __device__ __forceinline__ uint32_t ordered(float f) {
@@ -191,16 +202,50 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, int bh, int row,
   }
 }
 
+// GEMM 1 epilogue with the Direct tile staged for a TMA store: this thread's 32 Direct
+// values (row `lane` of the warp's box, 16-byte chunks 4h .. 4h + 3 of the 128-byte box row,
+// placed at chunk ^ (lane & 7) as the 128-byte swizzle lays them out); the optional f32
+// affinity output is written directly. Min-max normalisation and the f16 hi/lo split use
+// epilogue_chunk instead.
+__device__ __forceinline__ void affinity_staged(const Params& p, int bh, int row, int col0, const uint32_t (&acc)[32],
+                                                uint8_t* box, int h, int lane) {
+  __align__(16) __half hv[32];
+  __align__(16) float dv[32];
+#pragma unroll
+  for (int c = 0; c < 32; ++c) {
+    const float d = direct_of(__uint_as_float(acc[c]) * p.alpha, p.normalization);
+    dv[c] = d;
+    hv[c] = __float2half_rn(d);
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    *reinterpret_cast<uint4*>(box + lane * 128 + 16 * ((4 * h + q) ^ (lane & 7))) =
+        *reinterpret_cast<const uint4*>(&hv[8 * q]);
+  if (p.affinity && row < p.M && col0 < p.M) {
+    float* dst = p.affinity + (static_cast<int64_t>(bh) * p.M + row) * p.M + col0;
+    if (col0 + 32 <= p.M && (p.M % 4 == 0)) {
+#pragma unroll
+      for (int c = 0; c < 32; c += 4) *reinterpret_cast<float4*>(dst + c) = *reinterpret_cast<float4*>(&dv[c]);
+    } else {
+      for (int c = 0; c < 32; ++c)
+        if (col0 + c < p.M) dst[c] = dv[c];
+    }
+  }
+}
+
 // Persistent tcgen05 GEMM. kMode = kAffinity: A = Qc (K-major), B = Kc (K-major).
 // kMode = kTriangle: A = Direct (K-major), B = Direct (MN-major), `segments` = 1 or 3.
 template <int kMode>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_a1,
                 const __grid_constant__ CUtensorMap map_b0, const __grid_constant__ CUtensorMap map_b1,
-                const Params p, uint32_t idesc) {
+                const __grid_constant__ CUtensorMap map_d, const Params p, uint32_t idesc) {
+  using R = Ring<kMode>;
+  constexpr int kStages = R::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint8_t* staging = smem + kStages * kStageBytes;  // GEMM 1 Direct boxes (1024-aligned)
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + R::kStagingBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
@@ -215,6 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     prefetch_tensormap(&map_a0);
     prefetch_tensormap(&map_b0);
+    if (kMode == kAffinity && p.direct_tma) prefetch_tensormap(&map_d);
     if (kMode == kTriangle && p.segments > 1) {
       prefetch_tensormap(&map_a1);
       prefetch_tensormap(&map_b1);
@@ -349,12 +395,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = tm * kTileM + quad * 32 + lane;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * kTileN;
       constexpr int kChunks = kTileN / 32 / 2;
+      // GEMM 1 with staged Direct: this warp's two boxes are free once the stores of its
+      // previous tile have read them
+      const bool staged = kMode == kAffinity && p.direct_tma;
+      uint8_t* wbox = staging + (warp - 2) * 2 * R::kBoxBytes;
+      if (staged) {
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+      }
 #pragma unroll 1
       for (int c = colhalf * kChunks; c < (colhalf + 1) * kChunks; ++c) {
         uint32_t r[32];
         tmem_ld32(taddr + c * 32, r);
         tmem_wait_ld();
         const int col0 = tn * kTileN + c * 32;
+        if constexpr (kMode == kAffinity) {
+          if (staged) {
+            uint8_t* box = wbox + ((c & 3) >> 1) * R::kBoxBytes;
+            affinity_staged(p, bh, row, col0, r, box, c & 1, lane);
+            if (c & 1) {
+              // rows and columns past M are clipped by the tensor map
+              fence_proxy_async_smem();
+              __syncwarp();
+              const int brow = tm * kTileM + quad * 32, bcol = tn * kTileN + (c >> 1) * 64;
+              if (lane == 0 && brow < p.M && bcol < p.M) {  // boxes wholly past M are skipped
+                tma_store_3d(&map_d, box, bcol, brow, bh);
+                bulk_commit_group();
+              }
+            }
+            continue;
+          }
+        }
         if (row < p.M && col0 < p.M) epilogue_chunk<kMode>(p, bh, row, col0, r, vmin_neg, vmax);
       }
       tc_fence_before_sync();
@@ -362,6 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&tempty[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
+    if (kMode == kAffinity && p.direct_tma && lane == 0) bulk_wait_all();  // boxes stay valid until stored
     if (kMode == kAffinity && p.normalization == CAB_NORM_MINMAX && cur_bh >= 0) {
       float a = vmax, b = vmin_neg;
 #pragma unroll
@@ -577,11 +649,22 @@ extern "C" int cab_frc(const void* q_coarse, const void* k_coarse, float* frc_ou
     if (int rc = make_tensor_map(&mb, tma_type(dtype), 3, k_coarse, dk, sq, boxb, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
     p.kblocks = static_cast<int32_t>((D + kTileK - 1) / kTileK);
     p.segments = 1;
+    // Direct (f16) leaves through staged TMA stores unless min-max normalisation needs the
+    // raw values first; boxes of 64 columns x 32 rows, clipped at M
+    CUtensorMap md{};
+    p.direct_tma = normalization != CAB_NORM_MINMAX ? 1 : 0;
+    if (p.direct_tma) {
+      uint64_t dd[3] = {static_cast<uint64_t>(M), static_cast<uint64_t>(M), static_cast<uint64_t>(BH)};
+      uint64_t sd[2] = {static_cast<uint64_t>(L.Mp) * 2, static_cast<uint64_t>(M * L.Mp) * 2};
+      uint32_t boxd[3] = {64, 32, 1};
+      if (int rc = make_tensor_map(&md, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, p.direct_hi, dd, sd, boxd, CU_TENSOR_MAP_SWIZZLE_128B))
+        return rc;
+    }
     const int tiles = p.BH * p.tiles_m * p.tiles_n;
     const int grid = std::min(tiles, sms);
     const uint32_t idesc = make_idesc_f16(kTileM, kTileN, dtype == CAB_DTYPE_BF16 ? 1 : 0, 0, 0);
-    cudaFuncSetAttribute(gemm_kernel<kAffinity>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    gemm_kernel<kAffinity><<<grid, kThreads, kSmemBytes, st>>>(ma, ma, mb, mb, p, idesc);
+    cudaFuncSetAttribute(gemm_kernel<kAffinity>, cudaFuncAttributeMaxDynamicSharedMemorySize, Ring<kAffinity>::kSmem);
+    gemm_kernel<kAffinity><<<grid, kThreads, Ring<kAffinity>::kSmem, st>>>(ma, ma, mb, mb, md, p, idesc);
     if (int rc = check_launch("gemm_kernel<affinity>")) return rc;
   }
   if (p.minmax) {
@@ -612,8 +695,8 @@ extern "C" int cab_frc(const void* q_coarse, const void* k_coarse, float* frc_ou
     const int tiles = p.BH * p.tiles_m * p.tiles_n;
     const int grid = std::min(tiles, sms);
     const uint32_t idesc = make_idesc_f16(kTileM, kTileN, 0, 0, 1);
-    cudaFuncSetAttribute(gemm_kernel<kTriangle>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    gemm_kernel<kTriangle><<<grid, kThreads, kSmemBytes, st>>>(a0, a1, b0, b1, p, idesc);
+    cudaFuncSetAttribute(gemm_kernel<kTriangle>, cudaFuncAttributeMaxDynamicSharedMemorySize, Ring<kTriangle>::kSmem);
+    gemm_kernel<kTriangle><<<grid, kThreads, Ring<kTriangle>::kSmem, st>>>(a0, a1, b0, b1, a0, p, idesc);
     if (int rc = check_launch("gemm_kernel<triangle>")) return rc;
   }
   return CAB_OK;
