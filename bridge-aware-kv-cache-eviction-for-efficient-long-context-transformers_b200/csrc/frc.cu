@@ -49,15 +49,18 @@ constexpr float kEps = 1e-8f;
 
 enum Mode { kAffinity = 0, kTriangle = 1 };
 
-// Shared memory per mode. GEMM 1 (K = D <= 128, one or two K blocks per tile) runs a
-// 2-stage ring and stages its f16 Direct tile for TMA stores: each epilogue warp owns two
-// 32-row x 64-column boxes (128-byte rows, 128-byte swizzle) = 8 KB. GEMM 2 runs 4 stages.
+// Shared memory per mode. Both epilogues leave through TMA stores staged in 4 KB boxes of
+// 32 rows x 128 bytes (128-byte swizzle). GEMM 1 (K = D <= 128, one or two K blocks per
+// tile) runs a 2-stage ring and gives each epilogue warp two f16 Direct boxes (32 x 64);
+// GEMM 2 runs 4 stages and gives each epilogue warp one f32 F box (32 x 32), reused per
+// 32-column chunk once its previous store has read it.
 template <int kMode>
 struct Ring {
   static constexpr int kStages = kMode == kAffinity ? 2 : frc::kStages;
-  static constexpr int kBoxBytes = 32 * 64 * 2;
-  static constexpr int kStagingBytes = kMode == kAffinity ? kEpiWarps * 2 * kBoxBytes : 0;
+  static constexpr int kBoxBytes = 32 * 128;
+  static constexpr int kStagingBytes = kEpiWarps * (kMode == kAffinity ? 2 : 1) * kBoxBytes;
   static constexpr int kSmem = kStages * kStageBytes + kStagingBytes + 1024 /*align slack*/ + 256 /*barriers*/;
+  static_assert(kSmem <= 232448, "shared memory per CTA exceeded");
 };
 
 struct Params {
@@ -74,6 +77,7 @@ struct Params {
   float* affinity;    // [BH, M, M] or null
   float* redundancy;  // [BH, M, M] or null
   int32_t direct_tma;  // GEMM 1: Direct (hi only) leaves through staged TMA stores
+  int32_t frc_tma;     // GEMM 2: F leaves through staged TMA stores (M % 4 == 0)
 };
 
 __device__ __forceinline__ uint32_t ordered(float f) {
@@ -233,6 +237,40 @@ __device__ __forceinline__ void affinity_staged(const Params& p, int bh, int row
   }
 }
 
+// GEMM 2 epilogue with the F chunk staged for a TMA store: F = frc_of(Direct, T) of this
+// thread's 32 columns (row `lane` of the warp's 32 x 32 f32 box, 16-byte chunk q placed at
+// q ^ (lane & 7)); the optional T output is written directly.
+__device__ __forceinline__ void triangle_staged(const Params& p, int bh, int row, int col0, const uint32_t (&acc)[32],
+                                                uint8_t* box, int lane) {
+  const bool live = row < p.M && col0 < p.M;
+  const int64_t rbase = static_cast<int64_t>(bh) * p.M + row;
+  __align__(16) __half hv[32];
+  if (live && col0 + 32 <= p.M) {
+    const __half* dh = p.direct_hi + rbase * p.Mp + col0;
+#pragma unroll
+    for (int c = 0; c < 32; c += 8) *reinterpret_cast<uint4*>(&hv[c]) = *reinterpret_cast<const uint4*>(dh + c);
+  } else {
+    const __half* dh = p.direct_hi + rbase * p.Mp + col0;
+    for (int c = 0; c < 32; ++c) hv[c] = (live && col0 + c < p.M) ? dh[c] : __float2half(0.f);
+  }
+  __align__(16) float fv[32];
+  __align__(16) float tv[32];
+#pragma unroll
+  for (int c = 0; c < 32; ++c) {
+    const float t = __uint_as_float(acc[c]) * p.alpha;
+    tv[c] = t;
+    fv[c] = frc_of(__half2float(hv[c]), t, p.lambda, p.formula);
+  }
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    *reinterpret_cast<uint4*>(box + lane * 128 + 16 * (q ^ (lane & 7))) = *reinterpret_cast<const uint4*>(&fv[4 * q]);
+  if (p.redundancy && live) {
+    float* tdst = p.redundancy + rbase * p.M + col0;
+    for (int c = 0; c < 32; ++c)
+      if (col0 + c < p.M) tdst[c] = tv[c];
+  }
+}
+
 // Persistent tcgen05 GEMM. kMode = kAffinity: A = Qc (K-major), B = Kc (K-major).
 // kMode = kTriangle: A = Direct (K-major), B = Direct (MN-major), `segments` = 1 or 3.
 template <int kMode>
@@ -260,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     prefetch_tensormap(&map_a0);
     prefetch_tensormap(&map_b0);
-    if (kMode == kAffinity && p.direct_tma) prefetch_tensormap(&map_d);
+    if ((kMode == kAffinity && p.direct_tma) || (kMode == kTriangle && p.frc_tma)) prefetch_tensormap(&map_d);
     if (kMode == kTriangle && p.segments > 1) {
       prefetch_tensormap(&map_a1);
       prefetch_tensormap(&map_b1);
@@ -397,8 +435,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr int kChunks = kTileN / 32 / 2;
       // GEMM 1 with staged Direct: this warp's two boxes are free once the stores of its
       // previous tile have read them
-      const bool staged = kMode == kAffinity && p.direct_tma;
-      uint8_t* wbox = staging + (warp - 2) * 2 * R::kBoxBytes;
+      const bool staged = kMode == kAffinity ? p.direct_tma != 0 : p.frc_tma != 0;
+      uint8_t* wbox = staging + (warp - 2) * (kMode == kAffinity ? 2 : 1) * R::kBoxBytes;
       if (staged) {
         if (lane == 0) bulk_wait_read_all();
         __syncwarp();
@@ -425,6 +463,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             continue;
           }
+        } else {
+          if (staged) {
+            if (c != colhalf * kChunks) {  // the box is reused: its previous store must have read it
+              if (lane == 0) bulk_wait_read_all();
+              __syncwarp();
+            }
+            triangle_staged(p, bh, row, col0, r, wbox, lane);
+            fence_proxy_async_smem();
+            __syncwarp();
+            const int brow = tm * kTileM + quad * 32;
+            if (lane == 0 && brow < p.M && col0 < p.M) {  // clipped at M by the tensor map
+              tma_store_3d(&map_d, wbox, col0, brow, bh);
+              bulk_commit_group();
+            }
+            continue;
+          }
         }
         if (row < p.M && col0 < p.M) epilogue_chunk<kMode>(p, bh, row, col0, r, vmin_neg, vmax);
       }
@@ -433,7 +487,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&tempty[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
-    if (kMode == kAffinity && p.direct_tma && lane == 0) bulk_wait_all();  // boxes stay valid until stored
+    if (((kMode == kAffinity && p.direct_tma) || (kMode == kTriangle && p.frc_tma)) && lane == 0)
+      bulk_wait_all();  // boxes stay valid until stored
     if (kMode == kAffinity && p.normalization == CAB_NORM_MINMAX && cur_bh >= 0) {
       float a = vmax, b = vmin_neg;
 #pragma unroll
@@ -692,11 +747,22 @@ extern "C" int cab_frc(const void* q_coarse, const void* k_coarse, float* frc_ou
     p.kblocks = static_cast<int32_t>((M + kTileK - 1) / kTileK);
     p.segments = split ? 3 : 1;
     p.alpha = redundancy_scale == CAB_RED_SCALE_INV_M ? 1.0f / static_cast<float>(M) : 1.0f;
+    // F leaves through staged TMA stores (32 x 32 f32 boxes, clipped at M) when its rows are
+    // 16-byte multiples and there is no f16 lo part to add
+    CUtensorMap mf{};
+    p.frc_tma = (M % 4 == 0 && !split) ? 1 : 0;
+    if (p.frc_tma) {
+      uint64_t df[3] = {static_cast<uint64_t>(M), static_cast<uint64_t>(M), static_cast<uint64_t>(BH)};
+      uint64_t sf[2] = {static_cast<uint64_t>(M) * 4, static_cast<uint64_t>(M * M) * 4};
+      uint32_t boxf[3] = {32, 32, 1};
+      if (int rc = make_tensor_map(&mf, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, frc_out, df, sf, boxf, CU_TENSOR_MAP_SWIZZLE_128B))
+        return rc;
+    }
     const int tiles = p.BH * p.tiles_m * p.tiles_n;
     const int grid = std::min(tiles, sms);
     const uint32_t idesc = make_idesc_f16(kTileM, kTileN, 0, 0, 1);
     cudaFuncSetAttribute(gemm_kernel<kTriangle>, cudaFuncAttributeMaxDynamicSharedMemorySize, Ring<kTriangle>::kSmem);
-    gemm_kernel<kTriangle><<<grid, kThreads, Ring<kTriangle>::kSmem, st>>>(a0, a1, b0, b1, a0, p, idesc);
+    gemm_kernel<kTriangle><<<grid, kThreads, Ring<kTriangle>::kSmem, st>>>(a0, a1, b0, b1, p.frc_tma ? mf : a0, p, idesc);
     if (int rc = check_launch("gemm_kernel<triangle>")) return rc;
   }
   return CAB_OK;
