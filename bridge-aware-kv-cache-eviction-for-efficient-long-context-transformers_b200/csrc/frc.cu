@@ -7,10 +7,12 @@
 //                                                       (GEMM 2 epilogue)
 //
 // Both GEMMs run in one persistent, warp-specialised kernel template: warp 0 issues TMA
-// loads into a 4-stage shared-memory ring (128-byte swizzle), one thread of warp 1 issues
-// tcgen05.mma (M=128, N=256, K=16) into a double-buffered TMEM accumulator (2 x 256
-// columns), and warps 2-5 drain the other accumulator buffer through tcgen05.ld and run
-// the epilogue, so the epilogue of one 128x256 tile overlaps the main loop of the next.
+// loads into a shared-memory ring (128-byte swizzle; 2 stages for GEMM 1, 4 for GEMM 2),
+// one thread of warp 1 issues tcgen05.mma (M=128, N=256, K=16) into a double-buffered TMEM
+// accumulator (2 x 256 columns), and warps 2-9 (two per TMEM lane quadrant) drain the other
+// accumulator buffer through tcgen05.ld and run the epilogue, so the epilogue of one
+// 128x256 tile overlaps the main loop of the next. The epilogues stage Direct (GEMM 1) and
+// F (GEMM 2) in swizzled shared-memory boxes and write them with TMA stores.
 // GEMM 2 reads Direct through two tensor maps of the same buffer: K-major for the A
 // operand, MN-major (N contiguous) for the B operand, so no transpose is materialised.
 //
@@ -282,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kStages = R::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* staging = smem + kStages * kStageBytes;  // GEMM 1 Direct boxes (1024-aligned)
+  uint8_t* staging = smem + kStages * kStageBytes;  // epilogue store boxes (1024-aligned)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + R::kStagingBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
@@ -433,8 +435,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = tm * kTileM + quad * 32 + lane;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * kTileN;
       constexpr int kChunks = kTileN / 32 / 2;
-      // GEMM 1 with staged Direct: this warp's two boxes are free once the stores of its
-      // previous tile have read them
+      // staged epilogue: this warp's boxes are free once the stores of its previous tile
+      // have read them
       const bool staged = kMode == kAffinity ? p.direct_tma != 0 : p.frc_tma != 0;
       uint8_t* wbox = staging + (warp - 2) * (kMode == kAffinity ? 2 : 1) * R::kBoxBytes;
       if (staged) {
