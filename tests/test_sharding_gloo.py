@@ -122,3 +122,28 @@ def test_unit_inputs_equal_whole_batch_slices():
     qu, ku, vu = synthetic.make_unit_qkv(units, 2, 96, 8, torch.float32, seed=3)
     assert torch.equal(qu[0, 0:2], q[0, 2:4]) and torch.equal(qu[0, 2:4], q[1, 0:2])
     assert torch.equal(ku[0, 0], k[0, 1]) and torch.equal(vu[0, 1], v[1, 0])
+
+
+def test_bench_strong_plan_covers_units_evenly():
+    """bench.py's strong-scaling plan (one layer's B x Hkv units over N ranks, two chunks per
+    rank): every unit exactly once, equal shares where N divides the unit count, chunks that
+    tile each rank's units."""
+    import importlib.util
+    from pathlib import Path
+    spec = importlib.util.spec_from_file_location("bench_mod", Path(__file__).resolve().parents[1] / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    for name in ("ns", "c2", "c5"):
+        cfg = bench.CONFIGS[name]
+        n_units = cfg["B"] * cfg["Hkv"]
+        for world in (2, 4, 8):
+            seen = []
+            for rank in range(world):
+                lcfg, units, chunks = bench.shard_plan(cfg, rank, world, "strong")
+                assert lcfg["Hkv"] == len(units) and lcfg["Hq"] == len(units) * (cfg["Hq"] // cfg["Hkv"])
+                assert chunks[0][0] == 0 and chunks[-1][1] == len(units)
+                assert all(a[1] == b[0] for a, b in zip(chunks, chunks[1:]))
+                if n_units % world == 0:
+                    assert len(units) == n_units // world
+                seen += [b * cfg["Hkv"] + h for b, h in units]
+            assert sorted(seen) == list(range(n_units))
