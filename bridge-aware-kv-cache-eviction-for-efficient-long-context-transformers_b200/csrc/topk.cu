@@ -62,10 +62,12 @@ __device__ __forceinline__ uint32_t warp_excl_scan(uint32_t v, int lane, uint32_
 
 // Key of candidate j of row i. diag: 0 = ordinary, 1 = forced (always taken), 2 = excluded.
 // `taken` (a bitmap, or null) excludes candidates already chosen by an earlier phase.
+// kCheckN: candidates j >= ncand (causal rows) are excluded; without it every j < M is one.
+template <bool kCheckN>
 __device__ __forceinline__ uint32_t key_at(float f, int j, int i, int ncand, bool high, int diag,
                                            const uint32_t* taken) {
   uint32_t key = to_key(f, high);
-  if (j >= ncand) key = 0u;
+  if (kCheckN && j >= ncand) key = 0u;
   if (taken && ((taken[j >> 5] >> (j & 31)) & 1u)) key = 0u;
   if (diag != 0 && j == i) key = diag == 1 ? 0xFFFFFFFFu : 0u;
   return key;
@@ -74,6 +76,7 @@ __device__ __forceinline__ uint32_t key_at(float f, int j, int i, int ncand, boo
 // Loads row `src` into the warp's key buffer (four 16-byte loads per lane in flight when
 // M % 4 == 0; the tail of the last 4-key group is excluded) and returns the warp-reduced
 // range [kmin, kmax] of the ordinary keys (neither excluded nor forced).
+template <bool kCheckN>
 __device__ __forceinline__ void load_row(const float* src, uint32_t* keys, int M, int row_words, int i,
                                          int ncand, bool high, int diag, const uint32_t* taken, int lane,
                                          uint32_t& kmin, uint32_t& kmax) {
@@ -99,10 +102,10 @@ __device__ __forceinline__ void load_row(const float* src, uint32_t* keys, int M
         const int j4 = base + 32 * u;
         if (j4 < M4) {
           uint4 kv;
-          kv.x = key_at(v[u].x, 4 * j4 + 0, i, ncand, high, diag, taken);
-          kv.y = key_at(v[u].y, 4 * j4 + 1, i, ncand, high, diag, taken);
-          kv.z = key_at(v[u].z, 4 * j4 + 2, i, ncand, high, diag, taken);
-          kv.w = key_at(v[u].w, 4 * j4 + 3, i, ncand, high, diag, taken);
+          kv.x = key_at<kCheckN>(v[u].x, 4 * j4 + 0, i, ncand, high, diag, taken);
+          kv.y = key_at<kCheckN>(v[u].y, 4 * j4 + 1, i, ncand, high, diag, taken);
+          kv.z = key_at<kCheckN>(v[u].z, 4 * j4 + 2, i, ncand, high, diag, taken);
+          kv.w = key_at<kCheckN>(v[u].w, 4 * j4 + 3, i, ncand, high, diag, taken);
           track(kv.x);
           track(kv.y);
           track(kv.z);
@@ -123,7 +126,7 @@ __device__ __forceinline__ void load_row(const float* src, uint32_t* keys, int M
       for (int u = 0; u < 8; ++u) {
         const int j = base + 32 * u;
         if (j < row_words) {
-          const uint32_t key = j < M ? key_at(v[u], j, i, ncand, high, diag, taken) : 0u;
+          const uint32_t key = j < M ? key_at<kCheckN>(v[u], j, i, ncand, high, diag, taken) : 0u;
           track(key);
           keys[j] = key;
         }
@@ -281,6 +284,8 @@ __device__ __forceinline__ int select_pass(const uint32_t* keys, int M, int M4, 
   return static_cast<int>(taken);
 }
 
+// kHybrid: a magnitude phase before the score phase; kCausal: row i has i + 1 candidates.
+template <bool kHybrid, bool kCausal>
 __global__ void __launch_bounds__(256, 3) topk_kernel(const Params p) {
   extern __shared__ __align__(16) uint32_t smem[];
   const int warp = threadIdx.x >> 5;
@@ -295,12 +300,12 @@ __global__ void __launch_bounds__(256, 3) topk_kernel(const Params p) {
   uint32_t* hist = keys + row_words;
   uint32_t* bits = hist + 256;  // hybrid: candidates taken by magnitude
   const bool high = p.select_high != 0;
-  const bool hybrid = p.mag != nullptr;
+  constexpr bool hybrid = kHybrid;
 
   for (int64_t row = static_cast<int64_t>(blockIdx.x) * p.warps + warp; row < p.rows;
        row += static_cast<int64_t>(gridDim.x) * p.warps) {
     const int i = static_cast<int>(row % M);
-    const int ncand = p.causal ? i + 1 : M;
+    const int ncand = kCausal ? i + 1 : M;
     const int kk = min(p.k, ncand);
     const int forced = (p.keep_diagonal && i < ncand) ? 1 : 0;
     int rest = kk - forced;  // budget beyond the forced diagonal
@@ -313,7 +318,7 @@ __global__ void __launch_bounds__(256, 3) topk_kernel(const Params p) {
       for (int w = lane; w < bm_words; w += 32) bits[w] = 0u;
       __syncwarp();
       if (k_mag > 0) {
-        load_row(p.mag + row * M, keys, M, row_words, i, ncand, true, forced ? 2 : 0, nullptr, lane, kmin, kmax);
+        load_row<kCausal>(p.mag + row * M, keys, M, row_words, i, ncand, true, forced ? 2 : 0, nullptr, lane, kmin, kmax);
         radix_threshold(keys, M4, hist, kmin, kmax, k_mag, lane, tau, take_eq);
         select_pass(keys, M, M4, tau, take_eq, nullptr, bits, nullptr, nullptr, lane);
       }
@@ -321,7 +326,7 @@ __global__ void __launch_bounds__(256, 3) topk_kernel(const Params p) {
     }
     // phase 2 (the only phase without magnitude scores): the rest by score, among the
     // candidates not yet taken, plus the forced diagonal
-    load_row(p.scores + row * M, keys, M, row_words, i, ncand, high, p.keep_diagonal ? 1 : 0,
+    load_row<kCausal>(p.scores + row * M, keys, M, row_words, i, ncand, high, p.keep_diagonal ? 1 : 0,
              hybrid ? bits : nullptr, lane, kmin, kmax);
     radix_threshold(keys, M4, hist, kmin, kmax, rest, lane, tau, take_eq);
     int32_t* out_idx = p.kv_idx + row * p.k;
@@ -449,8 +454,10 @@ static int launch_topk(const float* scores, const float* mag, double ratio, int3
   const int64_t ctas_needed = (p.rows + warps - 1) / warps;
   const int per_sm = std::max<int>(1, static_cast<int>((227 * 1024) / (smem + 1024)));
   const int grid = static_cast<int>(std::min<int64_t>(ctas_needed, (int64_t)current_sm_count() * per_sm));
-  cudaFuncSetAttribute(topk::topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  topk::topk_kernel<<<grid, 32 * warps, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  auto kern = mag ? (p.causal ? topk::topk_kernel<true, true> : topk::topk_kernel<true, false>)
+                 : (p.causal ? topk::topk_kernel<false, true> : topk::topk_kernel<false, false>);
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  kern<<<grid, 32 * warps, smem, static_cast<cudaStream_t>(stream)>>>(p);
   return check_launch("topk_kernel");
 }
 
