@@ -370,6 +370,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (lane == 0) {
         uint32_t gi = 0, kt = 0, vt = 0;
         bool ok = true;
+        // L2 priorities: K / V tiles are re-read by the other items of their head (kept),
+        // Q is read once per item (streamed); O is stored evict-first as well
+        const uint64_t pol_keep = l2_evict_last_policy(), pol_stream = l2_evict_first_policy();
         // Tile counts are read one item ahead and list entries one tile ahead, so no list
         // read sits between a free stage and its TMA issue.
         int T_next = static_cast<int64_t>(blockIdx.x) < p.items ? item_tiles<kDense>(p, blockIdx.x) : 0;
@@ -392,7 +395,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           mbar_arrive_expect_tx(&q_full[qs], C::kQBytes);
   #pragma unroll
           for (int a = 0; a < C::kAtoms; ++a)
-            tma_load_4d(sQ + qs * C::kQBytes + a * 16384, &qmap, &q_full[qs], 64 * a, 128 * pr, h, b);
+            tma_load_4d_hint(sQ + qs * C::kQBytes + a * 16384, &qmap, &q_full[qs], 64 * a, 128 * pr, h, b, pol_stream);
           ++gi;
           for (int t = 0; t < T; ++t) {
             const int j0 = kDense ? 2 * t : static_cast<int>(e0 & kIdxMask);
@@ -417,8 +420,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             uint8_t* dk = sK + ks * C::kKBytes;
   #pragma unroll
             for (int a = 0; a < C::kAtoms; ++a) {
-              tma_load_4d(dk + a * 16384, &kmap, &k_full[ks], 64 * a, 64 * j0, hk, b);
-              tma_load_4d(dk + a * 16384 + 8192, &kmap, &k_full[ks], 64 * a, 64 * j1, hk, b);
+              tma_load_4d_hint(dk + a * 16384, &kmap, &k_full[ks], 64 * a, 64 * j0, hk, b, pol_keep);
+              tma_load_4d_hint(dk + a * 16384 + 8192, &kmap, &k_full[ks], 64 * a, 64 * j1, hk, b, pol_keep);
             }
             ++kt;
             const int vs = vt % C::kVStages;
@@ -429,8 +432,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             uint8_t* dv = sV + vs * C::kVBytes;
   #pragma unroll
             for (int a = 0; a < C::kAtoms; ++a) {
-              tma_load_4d(dv + a * 16384, &vmap, &v_full[vs], 64 * a, 64 * j0, hk, b);
-              tma_load_4d(dv + a * 16384 + 8192, &vmap, &v_full[vs], 64 * a, 64 * j1, hk, b);
+              tma_load_4d_hint(dv + a * 16384, &vmap, &v_full[vs], 64 * a, 64 * j0, hk, b, pol_keep);
+              tma_load_4d_hint(dv + a * 16384 + 8192, &vmap, &v_full[vs], 64 * a, 64 * j1, hk, b, pol_keep);
             }
             ++vt;
           }
@@ -885,7 +888,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         __syncwarp();
         const int row0 = 128 * pr + 32 * quad;
         if (lane == 0 && row0 < p.Nq) {
-          tma_store_4d(&omap, wbox, kb * kHalfD, row0, h, b);
+          tma_store_4d_hint(&omap, wbox, kb * kHalfD, row0, h, b, l2_evict_first_policy());
           bulk_commit_group();
         }
         pend_q = qs;
