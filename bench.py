@@ -565,12 +565,12 @@ def flex_compare(q, k, v, layer, lcfg, args, peak):
 
 # dram__bytes_read.sum + dram__bytes_write.sum per attention launch, from ncu captures of
 # attn_tc_kernel<128, bf16, sparse> on the north_star shape with 4 of its 16 (b, h) units
-# (409.530 MB read + 117.187 MB written) and of attn_tc_kernel<64, bf16, sparse> in the
-# configs[2] layer with 1 of its 2 batches (500.599 MB read + 114.063 MB written). DRAM
+# (401.845 MB read + 108.673 MB written) and of attn_tc_kernel<64, bf16, sparse> in the
+# configs[2] layer with 1 of its 2 batches (478.420 MB read + 108.516 MB written). DRAM
 # traffic is per unit (each unit reads its own Q/K/V once and writes its own O), so the
 # full launches are scaled by 16 / 4 and by 2.
-ATTN_TRAFFIC_BYTES = {"ns": (409.530112e6 + 117.187328e6) * 4,
-                      "c3": (500.599296e6 + 114.062592e6) * 2}
+ATTN_TRAFFIC_BYTES = {"ns": (401.845248e6 + 108.672768e6) * 4,
+                      "c3": (478.419712e6 + 108.515840e6) * 2}
 
 
 # --------------------------------------------------------------------------- reference arm
