@@ -225,9 +225,9 @@ constexpr int kPvWarp = 2;
 constexpr int kTrackWarp = 3;
 constexpr int kFirstSoftmaxWarp = 4;
 constexpr int kAttnThreads = 32 * (kFirstSoftmaxWarp + kSoftmaxWarps);
-// Register split of the sparse kernel (setmaxnreg): warpgroup 0 (producer, issuers,
-// tracker) hands registers to the two softmax warpgroups (measured 4-5 % faster on B200
-// than the even 168 / 168 split). 128 x (kRegsLow + 2 x kRegsHigh) must not exceed the
+// Register split (setmaxnreg, both modes): warpgroup 0 (producer, issuers, tracker) hands
+// registers to the two softmax warpgroups (measured on B200 against the even 168 / 168
+// split: sparse 4-5 % faster, dense 7 % without and 2 % with column scores). 128 x (kRegsLow + 2 x kRegsHigh) must not exceed the
 // launch's 384 x 168; the host checks the kernel's register count before each launch.
 constexpr int kRegsLow = 72, kRegsHigh = 216;
 constexpr int kRegsNeeded = (128 * (kRegsLow + 2 * kRegsHigh) + kAttnThreads - 1) / kAttnThreads;
@@ -364,7 +364,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   if (warp < kFirstSoftmaxWarp) {
     // warpgroup 0: TMA producer, S issuer, PV issuer, PV-completion tracker
-    if constexpr (!kDense) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
     if (warp == 0) {
       // ------------------------------------------------------------ TMA producer (Q, K, V)
       if (lane == 0) {
@@ -567,7 +567,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       __syncwarp();
     }
   } else {
-    if constexpr (!kDense) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
     // ------------------------------------------------------------ softmax + epilogue
     // Warp w (4..11) owns TMEM lane quadrant w & 3 (rows 32*(w&3) .. +31 of the 128-row
     // tile) and key block kb = (w - 4) / 4 of every 128-key tile (columns 64*kb .. +63).
@@ -1048,7 +1048,7 @@ template <int D, bool kBF16, bool kDense>
 static int launch_tc(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const CUtensorMap& om,
                      const Params& p, int grid, cudaStream_t st) {
   auto kern = attn_tc_kernel<D, kBF16, kDense>;
-  if constexpr (!kDense) {
+  {
     // The softmax warpgroups raise their register limit with setmaxnreg from the pool the
     // CTA was launched with; a build that gave the kernel fewer registers would make that
     // wait forever, so it is refused here.
