@@ -147,3 +147,19 @@ def test_bench_strong_plan_covers_units_evenly():
                     assert len(units) == n_units // world
                 seen += [b * cfg["Hkv"] + h for b, h in units]
             assert sorted(seen) == list(range(n_units))
+
+
+def test_bench_peak_selection():
+    """bench.py divides by the burst bf16 peak for a short timed window or a run at full
+    clock, by the sustained one for a seconds-long window that settled under the power cap."""
+    import importlib.util
+    from pathlib import Path
+    spec = importlib.util.spec_from_file_location("bench_mod2", Path(__file__).resolve().parents[1] / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    burst, sus = 1647.4, 1408.2
+    assert bench.pick_peak({"sm_mhz": 1965.0, "sm_max_mhz": 1965.0}, 92.0, burst, sus)[0] == burst
+    assert bench.pick_peak({"sm_mhz": 1600.0, "sm_max_mhz": 1965.0}, 500.0, burst, sus)[0] == burst
+    assert bench.pick_peak({"sm_mhz": 1960.0, "sm_max_mhz": 1965.0}, 5000.0, burst, sus)[0] == burst
+    assert bench.pick_peak({"sm_mhz": 1600.0, "sm_max_mhz": 1965.0}, 5000.0, burst, sus)[0] == sus
+    assert bench.pick_peak({"sm_mhz": None, "sm_max_mhz": None}, 5000.0, burst, sus)[0] == sus
